@@ -1,0 +1,339 @@
+#!/usr/bin/env python
+"""Benchmark: data-parallel 3-layer MLP training loop (1024->4096->4096->10,
+global batch 65536, cross_entropy, SGD by rebind), TensorLang program executed
+by the B200 backend.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    torchrun --nproc-per-node N bench.py --gpus N ...      (one rank per GPU)
+
+One step = one iteration of the program's training loop over the global
+batch (forward, device backward, NCCL gradient all-reduce, fused SGD
+update), replayed from a captured CUDA graph.  The batch is split
+contiguously over the ranks (strong scaling: the global batch is fixed).
+Timing: CUDA events on the backend's stream around K steps, after W warm-up
+steps, with a host barrier and device sync on both sides; the reported time
+is the maximum over ranks.  The working set (x: 256 MiB, activations
+1 GiB each) exceeds the 126 MB L2, so no flush is needed between steps.
+
+Rank 0 prints one JSON line.  At one GPU it also reports the fused
+elementwise chain gelu(add(mult(x,s),b)) > 0 on [8192,8192] (GB/s against
+HBM) under "fused_op".  ``--impl reference`` times the reference's NumPy
+execution of the same step (the float32 oracle restatement of its kernels
+and autograd) on the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+B_GLOBAL, D_IN, D_H, N_CLS = 65536, 1024, 4096, 10
+FLOP_PER_STEP = 7_712_686_521_792  # fwd 3 GEMMs + dW 3 + dX of layers 2,3
+FUSED_N = 8192
+FUSED_BYTES = 805_371_904  # read x, write y and m, plus s and b
+
+
+def peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), float(d.get("bf16_tflops_sustained", 0)), "measured"
+    return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": float(np.median(sm)) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline: the reference's NumPy execution (float32 oracle restatement)
+# ---------------------------------------------------------------------------
+
+def cpu_mlp_step_time(rows: int, reps: int = 1):
+    from oracle import OracleProgram
+    from __graft_entry__ import load_package
+    tl = load_package()
+    pr = tl.programs
+    ast = pr.mlp3_train(B=rows, I=D_IN, H=D_H, C=N_CLS, epochs=1)
+    feeds = pr.mlp3_inputs(B=rows, I=D_IN, H=D_H, C=N_CLS, seed=0)
+    env = {k: {"shape": v} for k, v in tl.shapes.complete_env(ast, {}).items()}
+    times = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        OracleProgram(ast, env, dtype=np.float32, feeds=feeds).run()
+        times.append(time.perf_counter() - t0)
+    return min(times)
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    rows = args.cpu_rows
+    cores = os.cpu_count() or 1
+    for _ in range(max(1, args.warmup)):
+        cpu_mlp_step_time(rows)
+    samples = [cpu_mlp_step_time(rows) for _ in range(max(1, args.steps))]
+    t = float(np.mean(samples)) * (B_GLOBAL / rows)  # seconds per full-batch step
+    value = 1.0 / t
+    line = {
+        "impl": "reference", "metric": "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)",
+        "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": t * 1000.0, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL, "dims": [D_IN, D_H, D_H, N_CLS],
+                   "parallelism": "host numpy", "l2": "inputs larger than L2"},
+        "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cores, "kind": "port",
+                         "sample": f"one training step on {rows} of the {B_GLOBAL} rows, "
+                                   f"scaled x{B_GLOBAL // rows}; mean of {len(samples)}"},
+        "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+
+def time_events(tl, stream, fn, reps):
+    rt = tl.runtime
+    e0, e1 = rt.Event(), rt.Event()
+    e0.record(stream)
+    for _ in range(reps):
+        fn()
+    e1.record(stream)
+    rt.lib().tl_stream_sync(stream)
+    return e0.elapsed_ms(e1) / reps
+
+
+def fused_op_bench(tl, dev, reps=20):
+    """The fused elementwise chain on [8192,8192], GB/s of algorithmic traffic."""
+    pr = tl.programs
+    ast, feeds = pr.fused_chain(FUSED_N), pr.fused_chain_inputs(FUSED_N, seed=0)
+    P = tl.Program(ast, None, feeds=feeds, fetch=["y", "m"], device=dev)
+    P.prepare()
+    regions = [s for s in P._all_steps() if type(s).__name__ == "RegionStep"]
+    P.execute()
+    P.sync()
+    for _ in range(3):
+        P.execute()
+    ms = time_events(tl, P.stream, P.execute, reps)
+    hbm, _, _, src = peaks()
+    gbs = FUSED_BYTES / (ms * 1e-3) / 1e9
+    res = {"metric": "fused-op HBM GB/s (gelu(add(mult(x,s),b)) > 0, [8192,8192])",
+           "value": gbs, "unit": "GB/s", "ms_per_launch": ms, "kernels": len(regions),
+           "roofline": {"bound": "hbm", "achieved": gbs, "peak": hbm, "unit": "GB/s",
+                        "frac": gbs / hbm, "peak_source": src,
+                        "traffic": None, "algorithmic_bytes": FUSED_BYTES}}
+    P.free()
+    return res
+
+
+def run_ours(args, rank, world, local):
+    from __graft_entry__ import load_package
+    tl = load_package()
+    rt = tl.runtime
+    from tensor_lang_b200 import dp
+
+    dev = local
+    rt.Device.get(dev)
+    addr = os.environ.get("MASTER_ADDR", "127.0.0.1")
+    port = int(os.environ.get("TL_RDV_PORT", str(int(os.environ.get("MASTER_PORT", "29500")) + 17)))
+    rdv = dp.Rendezvous(rank, world, addr, port)
+    comm = dp.Communicator(rdv)
+
+    b = B_GLOBAL // world
+    r0, r1 = rank * b, (rank + 1) * b
+    pr = tl.programs
+    ast = pr.mlp3_train(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, epochs=1 + args.warmup + args.steps)
+    feeds = pr.mlp3_inputs(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, seed=0, rows=(r0, r1))
+    D = dp.DataParallelProgram(ast, None, comm, device=dev, feeds=feeds, fetch=["loss", "W3"])
+    P = D.program
+    P.prepare()
+    loop = P.loops[0]
+    stream = P.stream
+
+    # first iteration eagerly (counts kernel launches), then capture the graph
+    rt.launch_count(reset=True)
+    loop.run_eager()
+    launches_per_step = rt.launch_count()
+    loop.capture()
+    for _ in range(args.warmup):
+        loop.replay(1)
+    comm.wait(stream)
+    P.sync()
+
+    clocks = Clocks(dev)
+    rdv.barrier()
+    clocks.start()
+    ms = time_events(tl, stream, lambda: loop.replay(1), args.steps)
+    clk = clocks.stop()
+    rdv.barrier()
+    all_ms = rdv.gather(ms)
+
+    # e2e through the public API: host (pinned) inputs uploaded every step,
+    # the loss read back every step
+    xs, ts = feeds["x"], feeds["t"]
+    hx = rt.PinnedHost(xs.nbytes)
+    hx.array(xs.shape)[...] = xs
+    ht = rt.PinnedHost(ts.nbytes)
+    ht.array(ts.shape)[...] = ts
+    hl = rt.PinnedHost(4)
+    L = rt.lib()
+    px, pt, pl = P.ptr("x"), P.ptr("t"), P.ptr("loss")
+
+    def e2e_step():
+        rt.check(L.tl_memcpy_h2d(px, hx.ptr, xs.nbytes, stream), "h2d x")
+        rt.check(L.tl_memcpy_h2d(pt, ht.ptr, ts.nbytes, stream), "h2d t")
+        loop.replay(1)
+        rt.check(L.tl_memcpy_d2h(hl.ptr, pl, 4, stream), "d2h loss")
+
+    e2e_step()
+    P.sync()
+    rdv.barrier()
+    e2e_ms = time_events(tl, stream, e2e_step, max(1, min(args.steps, 10)))
+    all_e2e = rdv.gather(e2e_ms)
+
+    # dominant kernel: the hidden-layer GEMM (b x 4096 x 4096), timed alone
+    M, N, K = b, D_H, D_H
+    gemm = lambda: rt.check(L.tl_gemm(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("h2"),  # noqa: E731
+                                       N, P.ptr("b2"), 0, 0, stream), "gemm")
+    gemm()
+    P.sync()
+    g_ms = time_events(tl, stream, gemm, 5)
+    path = "tcgen05 split-TF32" if L.tl_gemm_path(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N,
+                                                  P.ptr("h2"), N) == 0 else "CUDA-core fp32"
+    loss = float(P.read("loss").reshape(-1)[0])
+
+    fused = None
+    if world == 1 and not args.no_fused:
+        fused = fused_op_bench(tl, dev)
+
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu:
+            rows = args.cpu_rows
+            t = cpu_mlp_step_time(rows) * (B_GLOBAL / rows)
+            cpu = {"value": 1.0 / t, "unit": "steps/s", "cores": os.cpu_count() or 1, "kind": "port",
+                   "sample": f"float32 NumPy oracle: one training step on {rows} of {B_GLOBAL} rows, "
+                             f"scaled x{B_GLOBAL // rows}"}
+        ms_max = max(all_ms)
+        hbm, bf16, bf16s, src = peaks()
+        tflops = 2.0 * M * N * K / (g_ms * 1e-3) / 1e12
+        line = {
+            "metric": "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)",
+            "value": 1000.0 / ms_max, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL,
+                       "per_gpu_batch": b, "dims": [D_IN, D_H, D_H, N_CLS],
+                       "parallelism": f"dp{world}", "gemm": path,
+                       "l2": "inputs larger than L2 (no flush)"},
+            "model_tflops": FLOP_PER_STEP / (ms_max * 1e-3) / 1e12,
+            "loss_rank0": loss,
+            "roofline": {"bound": "tensor", "kernel": f"GEMM {M}x{N}x{K} ({path})",
+                         "achieved": tflops, "peak": bf16, "unit": "TFLOP/s",
+                         "frac": tflops / bf16, "peak_source": f"{src} bf16 dense (burst)",
+                         "traffic": None,
+                         "frac_of_split_tf32_est": tflops / (bf16 / 2 / 3)},
+            "e2e": {"value": 1000.0 / max(all_e2e), "unit": "steps/s",
+                    "h2d_bytes_per_step": int(xs.nbytes + ts.nbytes) * world,
+                    "d2h_bytes_per_step": 4 * world},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "clocks": clk,
+            "cpu_baseline": cpu,
+        }
+        if fused is not None:
+            line["fused_op"] = fused
+        print(json.dumps(line), flush=True)
+    P.free()
+    comm.destroy()
+    rdv.close()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-rows", type=int, default=4096)
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-fused", action="store_true")
+    args = ap.parse_args()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world, local)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,231 @@
+/*
+ * tlb200.h -- C ABI of libtlb200.so, the B200 (sm_100a) execution backend
+ * for TensorLang programs.
+ *
+ * The reference lowers every `let` of a .tl program to one generated CUDA
+ * kernel plus an `extern "C" void launch_<op>_<name>(float*..., int...)`
+ * launcher (tensorlang/kernel_generator.py), compiles them with nvcc into a
+ * per-program kernel.so, and calls the launchers through ctypes from
+ * TensorCompiler._execute_single_kernel (tensorlang/compiler.py:365-673),
+ * with PyCUDA allocations (compiler.py:1492-1503) and a
+ * cudaDeviceSynchronize() inside every launcher.
+ *
+ * This library replaces that layer.  Conventions for every entry point:
+ *   - plain pointers and sizes, no C++ or framework types;
+ *   - every call returns an int status: 0 on success, a cudaError_t value
+ *     for CUDA failures, or one of the TL_ERR_* codes below;
+ *   - work is enqueued on the stream argument (a cudaStream_t passed as
+ *     void*; NULL selects the library's per-device stream) and never
+ *     synchronises the device;
+ *   - tensors are dense row-major float32 ("f32" in .tl types); index results
+ *     (argmax/argmin) are written as float values, as the reference does;
+ *   - kernels never allocate.  Entry points that need temporary device memory
+ *     take a `scratch` pointer whose minimum size is returned by the matching
+ *     *_scratch_bytes() query; the scratch must be zero-filled once when it
+ *     is first allocated (kernels leave it zeroed for the next call).
+ */
+#ifndef TLB200_H
+#define TLB200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- status codes (in addition to cudaError_t values) ------------------ */
+#define TL_OK                 0
+#define TL_ERR_INVALID_ARG    1001  /* bad size, null pointer, unsupported op */
+#define TL_ERR_ALIGNMENT      1002  /* pointer or stride violates a documented alignment */
+#define TL_ERR_JIT            1003  /* NVRTC compile or module load failed; see tl_jit_log */
+#define TL_ERR_NO_NCCL        1004  /* libnccl.so.2 could not be loaded */
+#define TL_ERR_NCCL           1005  /* an NCCL call failed; see tl_error_string */
+#define TL_ERR_TIMEOUT        1006  /* a bounded device or host wait gave up */
+#define TL_ERR_NOT_INIT       1007  /* tl_init not called for the current device */
+#define TL_ERR_UNSUPPORTED    1008  /* shape/stride combination this kernel does not take */
+
+/* ---- runtime: device, memory, streams, events, graphs ------------------
+ * Replaces pycuda.autoinit / driver.mem_alloc / memcpy_htod / memcpy_dtoh /
+ * DeviceAllocation.free used at compiler.py:1472-1503, 244-289, 680, 1666-1673.
+ */
+int  tl_init(int device);                       /* set device, create its stream and pool */
+int  tl_device_count(int* count);
+int  tl_device_info(int device, int* sm_count, int* cc_major, int* cc_minor,
+                    size_t* total_mem);
+const char* tl_error_string(int status);
+void* tl_default_stream(void);                  /* the current device's library stream */
+
+int  tl_malloc(void** ptr, size_t bytes, void* stream);   /* stream-ordered pool */
+int  tl_free(void* ptr, void* stream);
+int  tl_host_alloc(void** ptr, size_t bytes);             /* pinned host memory */
+int  tl_host_free(void* ptr);
+int  tl_memcpy_h2d(void* dst, const void* src, size_t bytes, void* stream);
+int  tl_memcpy_d2h(void* dst, const void* src, size_t bytes, void* stream);
+int  tl_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
+int  tl_memset(void* dst, int value, size_t bytes, void* stream);
+
+int  tl_stream_create(void** stream);
+int  tl_stream_destroy(void* stream);
+int  tl_stream_sync(void* stream);
+int  tl_device_sync(void);
+int  tl_event_create(void** event);
+int  tl_event_destroy(void* event);
+int  tl_event_record(void* event, void* stream);
+int  tl_event_elapsed_ms(void* start, void* end, float* ms);
+int  tl_stream_wait_event(void* stream, void* event);
+
+/* CUDA graph capture of a stream: replaces the reference's per-iteration
+ * kernel-by-kernel replay of a for-loop body (compiler.py:206-303). */
+int  tl_graph_begin(void* stream);
+int  tl_graph_end(void* stream, void** graph_exec);
+int  tl_graph_launch(void* graph_exec, void* stream);
+int  tl_graph_destroy(void* graph_exec);
+
+/* Number of kernels this library has launched on the calling thread since
+ * the last reset (graph replays are not counted). */
+int  tl_launch_counter(uint64_t* count, int reset);
+
+/* ---- fused elementwise regions (run-time compiled) ---------------------
+ * Replaces the per-op elementwise launchers: elementwise
+ * (kernel_generator.py:246-275), binary_broadcast (:281-348),
+ * binary_1d_broadcast (:354-377), binary_general_broadcast (:383-463),
+ * fill (:469-488), relu/sigmoid/tanh (:209-240, 531-558), greater/less/equal
+ * (:646-778) and the fused SGD update of the rebind pattern
+ * (compiler.py:309-347).  The host generates one CUDA kernel per fused
+ * region; NVRTC compiles it for sm_100a; the cubin is cached in memory and
+ * under `cache_dir` (may be NULL) keyed by `key`.
+ */
+int  tl_jit_compile(const char* source, const char* kernel_name, const char* key,
+                    const char* cache_dir, void** function);
+const char* tl_jit_log(void);                   /* last NVRTC log on this thread */
+int  tl_jit_launch(void* function, unsigned grid, unsigned block, unsigned smem,
+                   void** args, void* stream);
+
+/* ---- reductions -----------------------------------------------------------
+ * op codes for tl_reduce_*.
+ * Replaces sum (kernel_generator.py:784-882), mean (:888-989),
+ * max (:1246-1345), min (:1352-1453), argmax (:1459-1542), argmin (:1549-1578).
+ * Sums accumulate in float64 and round once; argmax/argmin return the first
+ * index of the extreme value (strict compare scan, as the reference's
+ * axis kernels do).
+ */
+#define TL_RED_SUM    0
+#define TL_RED_MEAN   1
+#define TL_RED_MAX    2
+#define TL_RED_MIN    3
+#define TL_RED_ARGMAX 4
+#define TL_RED_ARGMIN 5
+
+/* out[r] = op over in[r, :]          (axis=1 of a [rows, cols] tensor) */
+int  tl_reduce_rows(int op, const float* in, float* out, int64_t rows, int64_t cols,
+                    void* stream);
+/* out[c] = op over in[:, c]          (axis=0) */
+size_t tl_reduce_cols_scratch_bytes(int op, int64_t rows, int64_t cols);
+int  tl_reduce_cols(int op, const float* in, float* out, int64_t rows, int64_t cols,
+                    void* scratch, void* stream);
+/* out[0] = op over all n elements    (axis=None) */
+size_t tl_reduce_full_scratch_bytes(int op, int64_t n);
+int  tl_reduce_full(int op, const float* in, float* out, int64_t n,
+                    void* scratch, void* stream);
+
+/* ---- softmax and normalisation ---------------------------------------------
+ * softmax (kernel_generator.py:564-640): exp(x-max)/sum along the row.
+ * layer_norm (:1667-1810) and instance_norm (:2017-2061): population
+ * statistics, (x-mean)/sqrt(var+eps), no affine parameters.
+ * batch_norm (:1978-2011): running statistics per column.
+ */
+int  tl_softmax_rows(const float* in, float* out, int64_t rows, int64_t cols, void* stream);
+size_t tl_norm_cols_scratch_bytes(int64_t rows, int64_t cols);
+int  tl_layer_norm_rows(const float* in, float* out, int64_t rows, int64_t cols,
+                        float eps, void* stream);
+int  tl_layer_norm_cols(const float* in, float* out, int64_t rows, int64_t cols,
+                        float eps, void* scratch, void* stream);
+int  tl_batch_norm(const float* in, const float* running_mean, const float* running_var,
+                   float* out, int64_t rows, int64_t cols, float eps, void* stream);
+
+/* ---- losses -------------------------------------------------------------
+ * mse_loss (kernel_generator.py:1891-1943): mean((p-t)^2).
+ * cross_entropy (:1816-1885): class-index targets (float values clamped to
+ * [0, C-1]) when onehot == 0; one-hot targets [B, C] when onehot != 0.
+ * The probability is clamped to [1e-7, 1-1e-7] before -log.
+ */
+size_t tl_loss_scratch_bytes(int64_t n);
+int  tl_mse_loss(const float* pred, const float* target, float* out, int64_t n,
+                 void* scratch, void* stream);
+int  tl_cross_entropy(const float* probs, const float* target, float* out,
+                      int64_t batch, int64_t classes, int onehot,
+                      void* scratch, void* stream);
+
+/* ---- reverse-mode kernels (tensorlang/autograd.py on the device) --------- */
+/* softmax VJP along rows, autograd.py:563-580: dx = s*(g - sum(g*s)) */
+int  tl_softmax_backward_rows(const float* s, const float* g, float* dx,
+                              int64_t rows, int64_t cols, int accumulate, void* stream);
+/* cross_entropy VJP (autograd.py:691-704) fused with the softmax VJP that
+ * follows it: gp = (p - t) / divisor * upstream[0] (divisor = the global
+ * batch; upstream may be NULL for 1.0), written to dp when non-null, and
+ * dz = gp*p - p*sum(gp*p) written (or added) to dz.  Class-index targets
+ * (onehot == 0) use one-hot(t). */
+int  tl_ce_softmax_backward(const float* p, const float* target, int onehot,
+                            const float* upstream, float divisor,
+                            float* dp, float* dz, int64_t rows, int64_t cols,
+                            int accumulate, void* stream);
+/* layer_norm VJP along rows, autograd.py:649-674 */
+int  tl_layer_norm_backward_rows(const float* x, const float* g, float* dx, int64_t rows,
+                                 int64_t cols, float eps, int accumulate, void* stream);
+
+/* ---- data movement --------------------------------------------------------
+ * transpose (kernel_generator.py:1949-1972), slice (:1112-1240),
+ * concat (:2092-2132), reshape (:2067-2086, a copy).
+ */
+int  tl_transpose2d(const float* in, float* out, int64_t rows, int64_t cols, void* stream);
+int  tl_slice2d(const float* in, float* out, int64_t in_cols, int64_t row_start,
+                int64_t col_start, int64_t out_rows, int64_t out_cols, void* stream);
+int  tl_concat_rows(const float* a, const float* b, float* out, int64_t rows_a,
+                    int64_t rows_b, int64_t cols, void* stream);
+
+/* ---- GEMM -----------------------------------------------------------------
+ * Replaces matmul (kernel_generator.py:501-525) and linear (:1584-1661), and
+ * serves the matmul/linear VJPs (autograd.py:520-537, 619-646).
+ *   C[M,N] (+)= op(A)[M,K] @ op(B)[K,N] (+ bias[N]) (then epilogue)
+ * op(X) = X when trans == 0, X^T when trans != 0; leading dimensions in
+ * elements of the row-major storage.  f32 in, f32 out.  On sm_100a the
+ * product runs on tcgen05 tensor cores as split-TF32 (three TF32 products
+ * hi*hi + hi*lo + lo*hi with fp32 accumulation in tensor memory), which
+ * keeps fp32-level accuracy; shapes the TMA path cannot describe take a
+ * tiled fp32 CUDA-core path.
+ * epilogue: 0 none, 1 relu (y = max(0, y)).
+ * accumulate: 0 overwrite C, 1 C += result.
+ */
+#define TL_EPI_NONE 0
+#define TL_EPI_RELU 1
+int  tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+             const float* A, int64_t lda, const float* B, int64_t ldb,
+             float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
+             void* stream);
+/* Which path tl_gemm would take (0 tensor-core, 1 CUDA-core) for this call. */
+int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+                  const float* A, int64_t lda, const float* B, int64_t ldb,
+                  const float* C, int64_t ldc);
+/* Force the CUDA-core path (1) or restore automatic selection (0). */
+int  tl_gemm_force_simt(int force);
+
+/* ---- data-parallel gradient exchange (NCCL over NVLink) ------------------
+ * The reference has no multi-GPU path (README.md:583 lists it as future work);
+ * these back the data-parallel for-loop executor.  libnccl.so.2 is loaded on
+ * first use.  Communicators are created non-blocking; tl_nccl_wait polls for
+ * completion and asynchronous errors up to timeout_ms and returns
+ * TL_ERR_TIMEOUT (after aborting the communicator) if it passes.
+ */
+int  tl_nccl_unique_id(unsigned char id[128]);
+int  tl_nccl_comm_init(void** comm, int nranks, const unsigned char id[128], int rank,
+                       int timeout_ms);
+int  tl_nccl_allreduce_sum(void* comm, float* buf, size_t count, void* stream);
+int  tl_nccl_wait(void* comm, void* stream, int timeout_ms);
+int  tl_nccl_comm_destroy(void* comm);
+int  tl_nccl_comm_abort(void* comm);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TLB200_H */

@@ -1,0 +1,451 @@
+// Axis and full reductions: sum / mean / max / min / argmax / argmin.
+//
+// Replaces the reference's sum (kernel_generator.py:784-882), mean (:888-989),
+// max (:1246-1345), min (:1352-1453), argmax (:1459-1542), argmin (:1549-1578).
+// The reference runs one thread per output row/column with a sequential
+// float32 loop (uncoalesced for axis 1) and atomics for full reductions.
+// Here: axis 1 is one warp per row with 128-bit loads; axis 0 is column
+// stripes of 128-bit loads split into row chunks whose partials are combined
+// in a fixed order by the last chunk to finish; full reductions are
+// grid-stride blocks combined the same way.  Sums accumulate in float64 and
+// round once, so results do not depend on launch shape; argmax/argmin keep the
+// first index of the extreme value (the reference's strict `>`/`<` scan).
+#include <cfloat>
+#include <climits>
+
+#include "tl_common.cuh"
+
+namespace tl {
+namespace {
+
+constexpr int kAssumedSms = 148;      // planning constant for chunk counts
+constexpr int kFullMaxBlocks = 2048;  // upper bound of full-reduction blocks
+// Every scratch buffer starts with a fixed counter region; partials follow it,
+// so reductions of different kinds may share one scratch buffer in stream order.
+constexpr size_t kCounterBytes = 4096;
+constexpr unsigned kMaxColBlocks = kCounterBytes / 4;
+
+struct ArgVal {
+  float v;
+  int64_t i;  // INT64_MAX marks "no element seen"
+};
+
+template <bool LARGEST>
+__device__ __forceinline__ bool arg_better(float vo, int64_t io, float v, int64_t i) {
+  if (io == INT64_MAX) return false;
+  if (i == INT64_MAX) return true;
+  if (LARGEST ? (vo > v) : (vo < v)) return true;
+  return vo == v && io < i;
+}
+
+template <bool LARGEST>
+__device__ __forceinline__ void arg_take(float& v, int64_t& i, float x, int64_t ix) {
+  if (i == INT64_MAX || (LARGEST ? (x > v) : (x < v))) {
+    v = x;
+    i = ix;
+  }
+}
+
+template <bool LARGEST>
+__device__ __forceinline__ void warp_arg(float& v, int64_t& i) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float vo = __shfl_xor_sync(0xffffffffu, v, o);
+    int64_t io = __shfl_xor_sync(0xffffffffu, i, o);
+    if (arg_better<LARGEST>(vo, io, v, i)) {
+      v = vo;
+      i = io;
+    }
+  }
+}
+
+// ------------------------------------------------------------ axis = 1 ----
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restrict__ in,
+                                                          float* __restrict__ out, int64_t rows,
+                                                          int64_t cols) {
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const float* p = in + row * cols;
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+    double s = 0.0;
+    if constexpr (VEC) {
+      const int64_t n4 = cols >> 2;
+      int64_t i = lane;
+      for (; i + 96 < n4; i += 128) {
+        float4 a = ld_stream4(p + 4 * i), b = ld_stream4(p + 4 * (i + 32));
+        float4 c = ld_stream4(p + 4 * (i + 64)), d = ld_stream4(p + 4 * (i + 96));
+        s += (double)a.x; s += (double)a.y; s += (double)a.z; s += (double)a.w;
+        s += (double)b.x; s += (double)b.y; s += (double)b.z; s += (double)b.w;
+        s += (double)c.x; s += (double)c.y; s += (double)c.z; s += (double)c.w;
+        s += (double)d.x; s += (double)d.y; s += (double)d.z; s += (double)d.w;
+      }
+      for (; i < n4; i += 32) {
+        float4 a = ld_stream4(p + 4 * i);
+        s += (double)a.x; s += (double)a.y; s += (double)a.z; s += (double)a.w;
+      }
+    } else {
+      for (int64_t i = lane; i < cols; i += 32) s += (double)p[i];
+    }
+    s = warp_sum(s);
+    if (lane == 0) out[row] = (OP == TL_RED_MEAN) ? (float)(s / (double)cols) : (float)s;
+  } else if constexpr (OP == TL_RED_MAX || OP == TL_RED_MIN) {
+    float m = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+    if constexpr (VEC) {
+      const int64_t n4 = cols >> 2;
+      for (int64_t i = lane; i < n4; i += 32) {
+        float4 a = ld_stream4(p + 4 * i);
+        if (OP == TL_RED_MAX) m = fmaxf(fmaxf(fmaxf(m, a.x), fmaxf(a.y, a.z)), a.w);
+        else m = fminf(fminf(fminf(m, a.x), fminf(a.y, a.z)), a.w);
+      }
+    } else {
+      for (int64_t i = lane; i < cols; i += 32)
+        m = (OP == TL_RED_MAX) ? fmaxf(m, p[i]) : fminf(m, p[i]);
+    }
+    m = (OP == TL_RED_MAX) ? warp_max(m) : warp_min(m);
+    if (lane == 0) out[row] = m;
+  } else {
+    constexpr bool L = (OP == TL_RED_ARGMAX);
+    float v = 0.f;
+    int64_t ix = INT64_MAX;
+    if constexpr (VEC) {
+      const int64_t n4 = cols >> 2;
+      for (int64_t i = lane; i < n4; i += 32) {
+        float4 a = ld_stream4(p + 4 * i);
+        arg_take<L>(v, ix, a.x, 4 * i);
+        arg_take<L>(v, ix, a.y, 4 * i + 1);
+        arg_take<L>(v, ix, a.z, 4 * i + 2);
+        arg_take<L>(v, ix, a.w, 4 * i + 3);
+      }
+    } else {
+      for (int64_t i = lane; i < cols; i += 32) arg_take<L>(v, ix, p[i], i);
+    }
+    warp_arg<L>(v, ix);
+    if (lane == 0) out[row] = (float)ix;
+  }
+}
+
+// ------------------------------------------------------------ axis = 0 ----
+struct ColPlan {
+  int vec;      // 4 when each thread owns a float4 column group, else 1
+  int threads;  // block size
+  unsigned gx;  // column blocks
+  unsigned gy;  // row chunks
+  int64_t chunk;
+};
+
+ColPlan col_plan(int64_t rows, int64_t cols, bool vec_ok) {
+  ColPlan p;
+  p.vec = vec_ok ? 4 : 1;
+  p.threads = 256;
+  int64_t groups = cols / p.vec;
+  if (groups < 256) p.threads = (int)((groups + 31) / 32 * 32);
+  if (p.threads < 32) p.threads = 32;
+  p.gx = ceil_div_u(groups, p.threads);
+  int64_t want = (4LL * kAssumedSms + p.gx - 1) / p.gx;
+  int64_t maxy = rows < 1024 ? rows : 1024;
+  if (want > maxy) want = maxy;
+  if (want < 1) want = 1;
+  p.chunk = (rows + want - 1) / want;
+  p.gy = (unsigned)((rows + p.chunk - 1) / p.chunk);
+  return p;
+}
+
+size_t col_partial_bytes(int op) { return (op == TL_RED_ARGMAX || op == TL_RED_ARGMIN) ? 16 : 8; }
+
+// Column reduction with fixed-order combine.  scratch layout:
+//   [0, 4*gx) unsigned counters (padded to 256 B) | partials[gy][cols]
+template <int OP, int VEC>
+__global__ void __launch_bounds__(256) reduce_cols_kernel(const float* __restrict__ in,
+                                                          float* __restrict__ out, int64_t rows,
+                                                          int64_t cols, int64_t chunk,
+                                                          unsigned* counters, void* partials) {
+  constexpr bool ARG = (OP == TL_RED_ARGMAX || OP == TL_RED_ARGMIN);
+  constexpr bool L = (OP == TL_RED_ARGMAX);
+  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // column group
+  const int64_t c0 = g * VEC;
+  const bool active = c0 < cols;
+  const int64_t r0 = (int64_t)blockIdx.y * chunk;
+  int64_t r1 = r0 + chunk;
+  if (r1 > rows) r1 = rows;
+
+  double s[VEC];
+  float m[VEC];
+  int64_t ix[VEC];
+#pragma unroll
+  for (int k = 0; k < VEC; ++k) {
+    s[k] = 0.0;
+    m[k] = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+    ix[k] = INT64_MAX;
+  }
+  if (active) {
+    for (int64_t r = r0; r < r1; ++r) {
+      float x[VEC];
+      if constexpr (VEC == 4) {
+        float4 a = ld_stream4(in + r * cols + c0);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+      } else {
+        x[0] = in[r * cols + c0];
+      }
+#pragma unroll
+      for (int k = 0; k < VEC; ++k) {
+        if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) s[k] += (double)x[k];
+        else if constexpr (OP == TL_RED_MAX) m[k] = fmaxf(m[k], x[k]);
+        else if constexpr (OP == TL_RED_MIN) m[k] = fminf(m[k], x[k]);
+        else arg_take<L>(m[k], ix[k], x[k], r);
+      }
+    }
+    // write this chunk's partials
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      int64_t c = c0 + k;
+      size_t off = (size_t)blockIdx.y * cols + c;
+      if constexpr (ARG) {
+        ((float*)partials)[2 * (2 * off)] = m[k];
+        ((int64_t*)partials)[2 * off + 1] = ix[k];
+      } else if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+        ((double*)partials)[off] = s[k];
+      } else {
+        ((float*)partials)[2 * off] = m[k];
+      }
+    }
+  }
+  __threadfence();
+  __shared__ unsigned is_last;
+  __syncthreads();
+  if (threadIdx.x == 0) is_last = (atomicAdd(&counters[blockIdx.x], 1u) == gridDim.y - 1);
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();
+  if (active) {
+#pragma unroll
+    for (int k = 0; k < VEC; ++k) {
+      int64_t c = c0 + k;
+      double ts = 0.0;
+      float tm = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+      int64_t ti = INT64_MAX;
+      for (unsigned y = 0; y < gridDim.y; ++y) {
+        size_t off = (size_t)y * cols + c;
+        if constexpr (ARG) {
+          float pv = __ldcg(&((float*)partials)[2 * (2 * off)]);
+          int64_t pi = __ldcg(&((int64_t*)partials)[2 * off + 1]);
+          if (arg_better<L>(pv, pi, tm, ti)) { tm = pv; ti = pi; }
+        } else if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+          ts += __ldcg(&((double*)partials)[off]);
+        } else {
+          float pv = __ldcg(&((float*)partials)[2 * off]);
+          tm = (OP == TL_RED_MAX) ? fmaxf(tm, pv) : fminf(tm, pv);
+        }
+      }
+      if constexpr (OP == TL_RED_SUM) out[c] = (float)ts;
+      else if constexpr (OP == TL_RED_MEAN) out[c] = (float)(ts / (double)rows);
+      else if constexpr (ARG) out[c] = (float)ti;
+      else out[c] = tm;
+    }
+  }
+  if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
+}
+
+// ------------------------------------------------------------ axis = None -
+template <int OP, bool VEC>
+__global__ void __launch_bounds__(256) reduce_full_kernel(const float* __restrict__ in,
+                                                          float* __restrict__ out, int64_t n,
+                                                          unsigned* counter, void* partials) {
+  constexpr bool ARG = (OP == TL_RED_ARGMAX || OP == TL_RED_ARGMIN);
+  constexpr bool L = (OP == TL_RED_ARGMAX);
+  __shared__ double sh_d[8];
+  __shared__ float sh_f[8];
+  __shared__ int64_t sh_i[8];
+  __shared__ unsigned is_last;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+
+  double s = 0.0;
+  float m = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+  int64_t ix = INT64_MAX;
+  if constexpr (VEC) {
+    const int64_t n4 = n >> 2;
+    for (int64_t i = tid; i < n4; i += stride) {
+      float4 a = ld_stream4(in + 4 * i);
+      if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+        s += (double)a.x; s += (double)a.y; s += (double)a.z; s += (double)a.w;
+      } else if constexpr (OP == TL_RED_MAX) {
+        m = fmaxf(fmaxf(fmaxf(m, a.x), fmaxf(a.y, a.z)), a.w);
+      } else if constexpr (OP == TL_RED_MIN) {
+        m = fminf(fminf(fminf(m, a.x), fminf(a.y, a.z)), a.w);
+      } else {
+        arg_take<L>(m, ix, a.x, 4 * i);
+        arg_take<L>(m, ix, a.y, 4 * i + 1);
+        arg_take<L>(m, ix, a.z, 4 * i + 2);
+        arg_take<L>(m, ix, a.w, 4 * i + 3);
+      }
+    }
+  } else {
+    for (int64_t i = tid; i < n; i += stride) {
+      float x = in[i];
+      if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) s += (double)x;
+      else if constexpr (OP == TL_RED_MAX) m = fmaxf(m, x);
+      else if constexpr (OP == TL_RED_MIN) m = fminf(m, x);
+      else arg_take<L>(m, ix, x, i);
+    }
+  }
+  // block combine (fixed order over warps)
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+    s = warp_sum(s);
+    if (lane == 0) sh_d[wid] = s;
+  } else if constexpr (ARG) {
+    warp_arg<L>(m, ix);
+    if (lane == 0) { sh_f[wid] = m; sh_i[wid] = ix; }
+  } else {
+    m = (OP == TL_RED_MAX) ? warp_max(m) : warp_min(m);
+    if (lane == 0) sh_f[wid] = m;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+      double t = 0.0;
+      for (int w = 0; w < nw; ++w) t += sh_d[w];
+      ((double*)partials)[blockIdx.x] = t;
+    } else if constexpr (ARG) {
+      float tv = sh_f[0];
+      int64_t ti = sh_i[0];
+      for (int w = 1; w < nw; ++w)
+        if (arg_better<L>(sh_f[w], sh_i[w], tv, ti)) { tv = sh_f[w]; ti = sh_i[w]; }
+      ((float*)partials)[4 * blockIdx.x] = tv;
+      ((int64_t*)partials)[2 * blockIdx.x + 1] = ti;
+    } else {
+      float t = sh_f[0];
+      for (int w = 1; w < nw; ++w) t = (OP == TL_RED_MAX) ? fmaxf(t, sh_f[w]) : fminf(t, sh_f[w]);
+      ((float*)partials)[2 * blockIdx.x] = t;
+    }
+    __threadfence();
+    is_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!is_last || threadIdx.x != 0) return;
+  __threadfence();
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+    double t = 0.0;
+    for (unsigned b = 0; b < gridDim.x; ++b) t += __ldcg(&((double*)partials)[b]);
+    out[0] = (OP == TL_RED_MEAN) ? (float)(t / (double)n) : (float)t;
+  } else if constexpr (ARG) {
+    float tv = 0.f;
+    int64_t ti = INT64_MAX;
+    for (unsigned b = 0; b < gridDim.x; ++b) {
+      float pv = __ldcg(&((float*)partials)[4 * b]);
+      int64_t pi = __ldcg(&((int64_t*)partials)[2 * b + 1]);
+      if (arg_better<L>(pv, pi, tv, ti)) { tv = pv; ti = pi; }
+    }
+    out[0] = (float)ti;
+  } else {
+    float t = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+    for (unsigned b = 0; b < gridDim.x; ++b) {
+      float pv = __ldcg(&((float*)partials)[2 * b]);
+      t = (OP == TL_RED_MAX) ? fmaxf(t, pv) : fminf(t, pv);
+    }
+    out[0] = t;
+  }
+  *counter = 0u;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+template <int OP>
+int launch_rows(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st) {
+  const unsigned grid = ceil_div_u(rows, 8);
+  if (cols % 4 == 0 && aligned16(in))
+    reduce_rows_kernel<OP, true><<<grid, 256, 0, st>>>(in, out, rows, cols);
+  else
+    reduce_rows_kernel<OP, false><<<grid, 256, 0, st>>>(in, out, rows, cols);
+  return after_launch();
+}
+
+template <int OP>
+int launch_cols(const float* in, float* out, int64_t rows, int64_t cols, void* scratch,
+                cudaStream_t st) {
+  const bool vec = (cols % 4 == 0) && aligned16(in);
+  ColPlan p = col_plan(rows, cols, vec);
+  if (p.gx > kMaxColBlocks) return TL_ERR_UNSUPPORTED;
+  unsigned* counters = (unsigned*)scratch;
+  void* partials = (char*)scratch + kCounterBytes;
+  dim3 grid(p.gx, p.gy);
+  if (vec)
+    reduce_cols_kernel<OP, 4><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+  else
+    reduce_cols_kernel<OP, 1><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+  return after_launch();
+}
+
+unsigned full_blocks(int64_t n) {
+  int64_t b = (n + 4LL * 256 - 1) / (4LL * 256);
+  int64_t cap = 8LL * sm_count();
+  if (cap > kFullMaxBlocks) cap = kFullMaxBlocks;
+  if (b > cap) b = cap;
+  if (b < 1) b = 1;
+  return (unsigned)b;
+}
+
+template <int OP>
+int launch_full(const float* in, float* out, int64_t n, void* scratch, cudaStream_t st) {
+  unsigned* counter = (unsigned*)scratch;
+  void* partials = (char*)scratch + kCounterBytes;
+  const unsigned grid = full_blocks(n);
+  if (n % 4 == 0 && aligned16(in))
+    reduce_full_kernel<OP, true><<<grid, 256, 0, st>>>(in, out, n, counter, partials);
+  else
+    reduce_full_kernel<OP, false><<<grid, 256, 0, st>>>(in, out, n, counter, partials);
+  return after_launch();
+}
+
+#define TL_DISPATCH_OP(op, F, ...)                          \
+  switch (op) {                                             \
+    case TL_RED_SUM: return F<TL_RED_SUM>(__VA_ARGS__);     \
+    case TL_RED_MEAN: return F<TL_RED_MEAN>(__VA_ARGS__);   \
+    case TL_RED_MAX: return F<TL_RED_MAX>(__VA_ARGS__);     \
+    case TL_RED_MIN: return F<TL_RED_MIN>(__VA_ARGS__);     \
+    case TL_RED_ARGMAX: return F<TL_RED_ARGMAX>(__VA_ARGS__); \
+    case TL_RED_ARGMIN: return F<TL_RED_ARGMIN>(__VA_ARGS__); \
+    default: return TL_ERR_INVALID_ARG;                     \
+  }
+
+}  // namespace
+}  // namespace tl
+
+extern "C" {
+
+int tl_reduce_rows(int op, const float* in, float* out, int64_t rows, int64_t cols, void* stream) {
+  if (!in || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARG;
+  cudaStream_t st = tl::stream_or_default(stream);
+  TL_DISPATCH_OP(op, tl::launch_rows, in, out, rows, cols, st);
+}
+
+size_t tl_reduce_cols_scratch_bytes(int op, int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  tl::ColPlan p = tl::col_plan(rows, cols, cols % 4 == 0);
+  tl::ColPlan q = tl::col_plan(rows, cols, false);
+  unsigned gy = p.gy > q.gy ? p.gy : q.gy;
+  return tl::kCounterBytes + (size_t)gy * (size_t)cols * tl::col_partial_bytes(op);
+}
+
+int tl_reduce_cols(int op, const float* in, float* out, int64_t rows, int64_t cols, void* scratch,
+                   void* stream) {
+  if (!in || !out || !scratch || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARG;
+  cudaStream_t st = tl::stream_or_default(stream);
+  TL_DISPATCH_OP(op, tl::launch_cols, in, out, rows, cols, scratch, st);
+}
+
+size_t tl_reduce_full_scratch_bytes(int op, int64_t n) {
+  (void)op;
+  (void)n;
+  return tl::kCounterBytes + (size_t)tl::kFullMaxBlocks * 16;
+}
+
+int tl_reduce_full(int op, const float* in, float* out, int64_t n, void* scratch, void* stream) {
+  if (!in || !out || !scratch || n <= 0) return TL_ERR_INVALID_ARG;
+  cudaStream_t st = tl::stream_or_default(stream);
+  TL_DISPATCH_OP(op, tl::launch_full, in, out, n, scratch, st);
+}
+
+}  // extern "C"

@@ -1,0 +1,281 @@
+"""Data-parallel execution of a training loop over the GPUs of one node.
+
+The reference has no multi-GPU path (README.md:583 lists it as future work).
+This module runs one process per GPU: the batch axis of the designated input
+tensors is split contiguously (rank r holds rows [r*B/P, (r+1)*B/P)), every
+rank holds full parameter replicas, and after each backward the gradients of
+the replicated tensors are summed across ranks with one NCCL all-reduce over
+NVLink (libtlb200 ``tl_nccl_allreduce_sum``).  The cross_entropy and mse_loss
+VJPs divide by the *global* batch (autograd.py:686,700), so the summed
+gradients equal the single-GPU ones and the replicated SGD update keeps the
+replicas identical.
+
+Host-side coordination (the NCCL unique id, barriers, gathering per-rank
+timings) goes over plain TCP sockets to rank 0; no framework is involved.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pickle
+import socket
+import struct
+import time
+from typing import Dict, Iterable, List, Optional, Sequence
+
+import numpy as np
+
+from . import runtime as rt
+from .engine import Program
+from .shapes import Shape, complete_env, expr_inputs, numel
+from .steps import Step
+
+# ops that consume the batch axis (their output is no longer per-example)
+_BATCH_REDUCING = {"mse_loss", "cross_entropy"}
+
+
+# ---------------------------------------------------------------------------
+# host rendezvous
+# ---------------------------------------------------------------------------
+
+class Rendezvous:
+    """Star-topology host channel: rank 0 accepts one socket per peer."""
+
+    def __init__(self, rank: int, world: int, addr: str = "127.0.0.1", port: int = 29517,
+                 timeout: float = 120.0):
+        self.rank, self.world = rank, world
+        self.peers: Dict[int, socket.socket] = {}
+        self.conn: Optional[socket.socket] = None
+        deadline = time.time() + timeout
+        if world == 1:
+            return
+        if rank == 0:
+            srv = socket.socket(socket.AF_INET, socket.SOCK_STREAM)
+            srv.setsockopt(socket.SOL_SOCKET, socket.SO_REUSEADDR, 1)
+            srv.bind((addr, port))
+            srv.listen(world)
+            srv.settimeout(max(1.0, deadline - time.time()))
+            while len(self.peers) < world - 1:
+                c, _ = srv.accept()
+                c.settimeout(timeout)
+                r = struct.unpack("!i", self._recv_exact(c, 4))[0]
+                self.peers[r] = c
+            srv.close()
+        else:
+            while True:
+                try:
+                    c = socket.create_connection((addr, port), timeout=5.0)
+                    break
+                except OSError:
+                    if time.time() > deadline:
+                        raise TimeoutError(f"rank {rank}: rendezvous with {addr}:{port} timed out")
+                    time.sleep(0.1)
+            c.settimeout(timeout)
+            c.sendall(struct.pack("!i", rank))
+            self.conn = c
+
+    @staticmethod
+    def _recv_exact(c: socket.socket, n: int) -> bytes:
+        buf = b""
+        while len(buf) < n:
+            chunk = c.recv(n - len(buf))
+            if not chunk:
+                raise ConnectionError("peer closed the rendezvous socket")
+            buf += chunk
+        return buf
+
+    def _send(self, c, obj):
+        data = pickle.dumps(obj)
+        c.sendall(struct.pack("!q", len(data)) + data)
+
+    def _recv(self, c):
+        n = struct.unpack("!q", self._recv_exact(c, 8))[0]
+        return pickle.loads(self._recv_exact(c, n))
+
+    def bcast(self, obj=None):
+        if self.world == 1:
+            return obj
+        if self.rank == 0:
+            for r in sorted(self.peers):
+                self._send(self.peers[r], obj)
+            return obj
+        return self._recv(self.conn)
+
+    def gather(self, obj) -> Optional[List]:
+        if self.world == 1:
+            return [obj]
+        if self.rank == 0:
+            out = [obj] + [None] * (self.world - 1)
+            for r in sorted(self.peers):
+                out[r] = self._recv(self.peers[r])
+            return out
+        self._send(self.conn, obj)
+        return None
+
+    def barrier(self):
+        self.gather(0)
+        self.bcast(0)
+
+    def close(self):
+        for c in list(self.peers.values()) + ([self.conn] if self.conn else []):
+            try:
+                c.close()
+            except OSError:
+                pass
+
+
+# ---------------------------------------------------------------------------
+# NCCL communicator
+# ---------------------------------------------------------------------------
+
+class Communicator:
+    def __init__(self, rdv: Rendezvous, timeout_ms: int = 120000):
+        self.rdv = rdv
+        self.world, self.rank = rdv.world, rdv.rank
+        self.timeout_ms = timeout_ms
+        self.handle = None
+        if self.world == 1:
+            return
+        L = rt.lib()
+        uid = ctypes.create_string_buffer(128)
+        if self.rank == 0:
+            rt.check(L.tl_nccl_unique_id(uid), "nccl_unique_id")
+        raw = rdv.bcast(uid.raw if self.rank == 0 else None)
+        uid = ctypes.create_string_buffer(raw, 128)
+        h = ctypes.c_void_p()
+        rt.check(L.tl_nccl_comm_init(ctypes.byref(h), self.world, uid, self.rank, timeout_ms),
+                 "nccl_comm_init")
+        self.handle = h.value
+
+    def wait(self, stream, timeout_ms: Optional[int] = None):
+        if self.handle:
+            rt.check(rt.lib().tl_nccl_wait(self.handle, stream,
+                                           self.timeout_ms if timeout_ms is None else timeout_ms),
+                     "nccl_wait")
+
+    def destroy(self):
+        if self.handle:
+            rt.lib().tl_nccl_comm_destroy(self.handle)
+            self.handle = None
+
+    def abort(self):
+        if self.handle:
+            rt.lib().tl_nccl_comm_abort(self.handle)
+            self.handle = None
+
+
+class AllReduce(Step):
+    """Sum the named gradients across ranks (one NCCL call per contiguous run)."""
+
+    def __init__(self, names: Sequence[str], comm: Communicator):
+        self.names = list(names)
+        self.comm = comm
+        self.reads, self.writes = list(names), list(names)
+        self.label = "allreduce:" + ",".join(names)
+
+    def bind(self, P):
+        L = rt.lib()
+        spans = []
+        for n in self.names:
+            p, cnt = P.ptr(n), numel(P.shapes[n])
+            if spans and spans[-1][0] + 4 * spans[-1][1] == p:
+                spans[-1][1] += cnt
+            else:
+                spans.append([p, cnt])
+        h, stream = self.comm.handle, P.stream
+
+        def run():
+            for p, cnt in spans:
+                rt.check(L.tl_nccl_allreduce_sum(h, p, cnt, stream), "nccl_allreduce")
+        return run
+
+
+# ---------------------------------------------------------------------------
+# sharding
+# ---------------------------------------------------------------------------
+
+def batch_derived(ast: list, sharded: Iterable[str]) -> set:
+    """Names whose leading axis is the (sharded) batch axis."""
+    derived = set(sharded)
+
+    def visit(nodes):
+        for n in nodes:
+            if n["type"] == "for":
+                visit(n["body"])
+            elif n["type"] == "let" and isinstance(n.get("expr"), dict):
+                e = n["expr"]
+                if e["type"] in _BATCH_REDUCING:
+                    continue
+                if e["type"] in ("sum", "mean", "max", "min", "argmax", "argmin") and \
+                        e.get("axis") in (None, 0):
+                    continue
+                if e["type"] == "linear":
+                    if e["args"][0] in derived:
+                        derived.add(n["name"])
+                    continue
+                if e["type"] == "matmul":
+                    if e["args"][0] in derived:
+                        derived.add(n["name"])
+                    continue
+                if any(i in derived for i in expr_inputs(e)):
+                    derived.add(n["name"])
+    visit(ast)
+    visit(ast)  # loop-carried names
+    return derived
+
+
+def shard_shapes(shapes: Dict[str, Shape], derived: set, world: int) -> Dict[str, Shape]:
+    local = dict(shapes)
+    for n in list(shapes):
+        base = n[:-5] if n.endswith("_grad") else n
+        if base in derived and shapes[n]:
+            B = shapes[n][0]
+            if B % world:
+                raise ValueError(f"batch {B} of {n} does not split over {world} ranks")
+            local[n] = (B // world,) + tuple(shapes[n][1:])
+    return local
+
+
+def loss_divisors(ast: list, shapes: Dict[str, Shape], derived: set) -> dict:
+    """Global batch (cross_entropy) / global element count (mse_loss) per loss."""
+    out = {}
+
+    def visit(nodes):
+        for n in nodes:
+            if n["type"] == "for":
+                visit(n["body"])
+            elif n["type"] == "let" and isinstance(n.get("expr"), dict):
+                e = n["expr"]
+                if e["type"] == "cross_entropy" and e["args"][0] in derived:
+                    out[("ce", n["name"])] = float(shapes[e["args"][0]][0])
+                elif e["type"] == "mse_loss" and e["args"][0] in derived:
+                    out[("mse", n["name"])] = float(numel(shapes[e["args"][0]]))
+    visit(ast)
+    return out
+
+
+class DataParallelProgram:
+    """A Program whose batch axis is split over ``comm.world`` GPUs."""
+
+    def __init__(self, ast: list, env: Optional[dict], comm: Communicator, *, device: int,
+                 feeds: Dict[str, np.ndarray], fetch: Optional[Sequence[str]] = None,
+                 sharded: Sequence[str] = ("x", "t"), use_graphs: bool = True):
+        self.comm = comm
+        gshapes = complete_env(ast, env or {})
+        self.derived = batch_derived(ast, sharded)
+        local = shard_shapes(gshapes, self.derived, comm.world)
+        divisors = loss_divisors(ast, gshapes, self.derived)
+        self.global_shapes = gshapes
+        self.replicated_grads: List[str] = []
+
+        def hook(prog, exposed):
+            names = [f"{n}_grad" for n in exposed if n not in self.derived]
+            self.replicated_grads = names
+            prog.arena_names = list(names)
+            return [AllReduce(names, comm)] if comm.world > 1 and names else []
+
+        self.program = Program(ast, None, device=device, feeds=feeds, fetch=fetch, shapes=local,
+                               divisors=divisors, grad_hook=hook, use_graphs=use_graphs)
+
+    def run(self):
+        return self.program.run()

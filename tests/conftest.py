@@ -36,3 +36,38 @@ def golden(name):
 
 def arr(j):
     return np.asarray(j["data"], dtype=np.float64).reshape(j["shape"])
+
+
+def assert_close(got, ref, rtol, name="", atol=None):
+    """|got - ref| <= rtol*|ref| + atol elementwise, atol = rtol * max|ref| unless given.
+
+    Near-zero entries of long sums and products cannot meet a pure relative
+    bound, so the absolute part is scaled to the tensor's magnitude.
+    """
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    assert got.shape == ref.shape, (name, got.shape, ref.shape)
+    if ref.size == 0:
+        return
+    scale = float(np.abs(ref).max())
+    if atol is None:
+        atol = rtol * scale
+    err = np.abs(got - ref)
+    bad = err > rtol * np.abs(ref) + atol
+    if bad.any():
+        i = int(np.argmax(err - (rtol * np.abs(ref) + atol)))
+        raise AssertionError(
+            f"{name}: {int(bad.sum())}/{ref.size} outside rtol={rtol} atol={atol:.3g}; "
+            f"worst at {np.unravel_index(i, ref.shape)}: got {got.flat[i]!r} ref {ref.flat[i]!r}")
+
+
+def gpu_available():
+    try:
+        tl = load_backend()
+        from tensor_lang_b200 import runtime as rt
+        import ctypes
+        n = ctypes.c_int(0)
+        rt.load_library().tl_device_count(ctypes.byref(n))
+        return n.value > 0
+    except Exception:
+        return False
