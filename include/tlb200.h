@@ -124,6 +124,20 @@ int  tl_reduce_rows(int op, const float* in, float* out, int64_t rows, int64_t c
 size_t tl_reduce_cols_scratch_bytes(int op, int64_t rows, int64_t cols);
 int  tl_reduce_cols(int op, const float* in, float* out, int64_t rows, int64_t cols,
                     void* scratch, void* stream);
+/* Same result as tl_reduce_cols, but allocates nothing and takes no scratch
+ * argument.  No counterpart in the reference: it exists for callers that
+ * cannot allocate device memory (a plugin inside a host framework that owns
+ * every device allocation, or a fixed-budget path that must not allocate
+ * while it runs).  Its scratch is a 1 MiB file-scope device array of the
+ * library, held by every GPU that loads the library until the process exits.
+ * cols may be at most 65280 for argmax/argmin and 130560 for the other ops
+ * ((1 MiB - 4 KiB) / 16 or / 8 bytes of partials per column); larger sizes
+ * return TL_ERR_INVALID_ARG without launching anything.  The first call on a device
+ * looks up the array's device address (cudaGetSymbolAddress) and should come
+ * before any stream capture.  All calls share the array: calls whose kernels
+ * overlap on the GPU race, so issue them in one stream order. */
+int  tl_reduce_cols_noalloc(int op, const float* in, float* out, int64_t rows, int64_t cols,
+                            void* stream);
 /* out[0] = op over all n elements    (axis=None) */
 size_t tl_reduce_full_scratch_bytes(int op, int64_t n);
 int  tl_reduce_full(int op, const float* in, float* out, int64_t n,

@@ -449,3 +449,81 @@ int tl_reduce_full(int op, const float* in, float* out, int64_t n, void* scratch
 }
 
 }  // extern "C"
+
+// ===================================================== no-allocation variant
+// Column reduction whose scratch is a file-scope device array instead of a
+// caller-provided buffer, for callers that cannot allocate device memory
+// (for example a plugin running inside a host framework that owns every
+// device allocation, or a fixed-budget path that must not allocate while it
+// runs).  The array is part of the module: every GPU that loads this library
+// holds it until process exit.  Every call shares it, so calls whose kernels
+// overlap on the GPU race; serialise them on one stream.
+#include <mutex>
+
+namespace tl {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB per device
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device.  In host code
+// the array's name is only a host-side stand-in, so the address must come
+// from cudaGetSymbolAddress, once per device, with that device current.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  TL_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return TL_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_addr[dev]) {
+    void* p = nullptr;
+    TL_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return TL_OK;
+}
+
+template <int OP>
+int launch_cols_noalloc(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st) {
+  const bool vec = (cols % 4 == 0) && aligned16(in);
+  ColPlan p = col_plan(rows, cols, vec);
+  if (p.gx > kMaxColBlocks) return TL_ERR_INVALID_ARG;
+  // fewer row chunks, so that the partials fit in the static array
+  const size_t per_chunk = (size_t)cols * col_partial_bytes(OP);
+  const size_t fit = (kNoAllocScratchBytes - kCounterBytes) / per_chunk;
+  if (fit < 1) return TL_ERR_INVALID_ARG;
+  if (p.gy > fit) {
+    p.chunk = (rows + (int64_t)fit - 1) / (int64_t)fit;
+    p.gy = (unsigned)((rows + p.chunk - 1) / p.chunk);
+  }
+  void* base = nullptr;
+  TL_TRY(noalloc_scratch(&base));
+  // the completion counters must start at zero; the partials need no clearing
+  TL_CUDA_TRY(cudaMemsetAsync(base, 0, (size_t)p.gx * sizeof(unsigned), st));
+  unsigned* counters = (unsigned*)base;
+  void* partials = (char*)base + kCounterBytes;
+  dim3 grid(p.gx, p.gy);
+  if (vec)
+    reduce_cols_kernel<OP, 4><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+  else
+    reduce_cols_kernel<OP, 1><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+  return after_launch();
+}
+
+}  // namespace
+}  // namespace tl
+
+extern "C" int tl_reduce_cols_noalloc(int op, const float* in, float* out, int64_t rows,
+                                      int64_t cols, void* stream) {
+  if (!in || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARG;
+  if (op < TL_RED_SUM || op > TL_RED_ARGMIN) return TL_ERR_INVALID_ARG;
+  // widest row whose single-chunk partials still fit in the static array
+  const int64_t max_cols =
+      (int64_t)((tl::kNoAllocScratchBytes - tl::kCounterBytes) / tl::col_partial_bytes(op));
+  if (cols > max_cols) return TL_ERR_INVALID_ARG;
+  cudaStream_t st = tl::stream_or_default(stream);
+  TL_DISPATCH_OP(op, tl::launch_cols_noalloc, in, out, rows, cols, st);
+}

@@ -78,6 +78,7 @@ _SIGS = [
     ("tl_reduce_rows", c_int, [c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     ("tl_reduce_cols_scratch_bytes", c_size_t, [c_int, c_int64, c_int64]),
     ("tl_reduce_cols", c_int, [c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p]),
+    ("tl_reduce_cols_noalloc", c_int, [c_int, c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
     ("tl_reduce_full_scratch_bytes", c_size_t, [c_int, c_int64]),
     ("tl_reduce_full", c_int, [c_int, c_void_p, c_void_p, c_int64, c_void_p, c_void_p]),
     ("tl_softmax_rows", c_int, [c_void_p, c_void_p, c_int64, c_int64, c_void_p]),
