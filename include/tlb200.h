@@ -221,8 +221,13 @@ int  tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
 int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                   const float* A, int64_t lda, const float* B, int64_t ldb,
                   const float* C, int64_t ldc);
-/* Force the CUDA-core path (1) or restore automatic selection (0). */
+/* Path selection: 0 automatic (tensor cores when the shape allows, the raw
+ * operand as the TF32 "hi" part); 1 force the CUDA-core path; 2 automatic,
+ * with hi and lo both rounded to TF32 explicitly in the pre-pass. */
 int  tl_gemm_force_simt(int force);
+/* Device-side error flag (TL_ERR_TIMEOUT after a bounded wait in a kernel
+ * gave up; 0 if none).  reset != 0 clears it. */
+int  tl_device_error(int* code, int reset);
 
 /* ---- data-parallel gradient exchange (NCCL over NVLink) ------------------
  * The reference has no multi-GPU path (README.md:583 lists it as future work);

@@ -19,6 +19,7 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
             int epilogue, cudaStream_t st);
 bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                 const float* B, int64_t ldb, const float* C, int64_t ldc);
+void gemm_set_split_mode(int mode);
 
 namespace {
 
@@ -169,7 +170,9 @@ int tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, cons
 }
 
 int tl_gemm_force_simt(int force) {
-  tl::g_force_simt = force != 0;
+  if (force < 0 || force > 2) return TL_ERR_INVALID_ARG;
+  tl::g_force_simt = force == 1;
+  tl::gemm_set_split_mode(force == 2 ? 1 : 0);
   return TL_OK;
 }
 

@@ -1,17 +1,588 @@
-// Split-TF32 GEMM on the sm_100a tensor cores (tcgen05 + TMEM + TMA).
-// Placeholder until the tensor-core kernel lands: no shape is routed here.
+// Split-TF32 GEMM on the sm_100a tensor cores: tcgen05.mma with the
+// accumulator in tensor memory, operands staged by TMA.
+//
+// Serves matmul (kernel_generator.py:501-525), linear (:1584-1661) and the
+// matmul/linear VJPs (autograd.py:520-537, 619-646), in float32:
+//   C[M,N] (+)= op(A)[M,K] @ op(B)[K,N] (+ bias[N]) (relu)
+//
+// fp32 accuracy from TF32 tensor cores: the tensor core reads an fp32
+// operand as TF32 by dropping the low 13 mantissa bits, so the raw operand
+// is the "hi" part; a pre-pass writes lo = x - trunc_tf32(x) (exact in fp32)
+// to a workspace, and each 8-deep k-step issues three MMAs, hi*hi + hi*lo +
+// lo*hi, accumulating in fp32 in TMEM (the dropped lo*lo term is ~2^-22
+// relative).
+//
+// One CTA computes a 128 x 256 tile with 10 warps:
+//   warp 0 lane 0   TMA producer (2-stage ring of hi/lo tiles of A and B)
+//   warp 1          TMEM allocation; lane 0 issues the MMAs
+//   warps 2-9       epilogue: drain each finished TMEM chunk into fp32
+//                   registers (round to nearest), then bias, relu,
+//                   accumulate, store
+// K-major operands (A as stored, B^T as stored) are one TMA box per tile in
+// the 128-byte swizzle; MN-major operands (A^T, and B stored [K][N]) are
+// 32-wide boxes, one per 32 rows of M or N, in the 128-byte swizzle with
+// 32-byte atoms (the layout tcgen05 requires for MN-major tf32).  No TMA
+// multicast is used.  Every mbarrier wait is bounded: on timeout the kernel
+// records TL_ERR_TIMEOUT in a device flag (tl_device_error) and falls
+// through to free its TMEM and exit.
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <vector>
+
 #include "tl_common.cuh"
 
 namespace tl {
 
-bool gemm_tc_ok(int, int, int64_t, int64_t, int64_t, const float*, int64_t, const float*, int64_t,
-                const float*, int64_t) {
+__device__ int g_device_error = 0;
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
+constexpr int KC = 2;                          // k-blocks per TMEM accumulation chunk
+constexpr int A_TILE = BM * BK * 4;            // 16 KB
+constexpr int B_TILE = BN * BK * 4;            // 32 KB
+constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // hi + lo of A and B: 96 KB
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int TMEM_COLS = 512;                 // two BN-wide accumulators, used alternately
+constexpr int EPI_WARPS = 8;                   // 2 per TMEM lane quarter, BN/2 columns each
+constexpr int THREADS = 64 + 32 * EPI_WARPS;   // producer warp, MMA warp, epilogue warps
+constexpr unsigned long long kWaitLimitNs = 2000000000ULL;  // 2 s: far above any normal wait
+
+// ---------------------------------------------------------------- PTX -----
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// Bounded wait: gives up after kWaitLimitNs, flags TL_ERR_TIMEOUT in the
+// device error word and returns false.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (;;) {
+    for (int i = 0; i < 256; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) break;
+  }
+  atomicExch(&g_device_error, TL_ERR_TIMEOUT);
   return false;
 }
-
-int gemm_tc(int, int, int64_t, int64_t, int64_t, const float*, int64_t, const float*, int64_t,
-            float*, int64_t, const float*, int, int, cudaStream_t) {
-  return TL_ERR_UNSUPPORTED;
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
+  // load and wait in one asm statement: the destination registers are only
+  // valid after tcgen05.wait::ld, so nothing may read them in between
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+      "%30, %31}, [%32];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Shared-memory matrix descriptor with the tcgen05 version bits.
+//   K-major operands:  128-byte swizzle (16-byte atoms, 8-row period), layout 2
+//   MN-major operands: 128-byte swizzle with 32-byte atoms (4-row period), layout 1
+//                      -- the only shared-memory layout tcgen05 accepts for
+//                      MN-major 32-bit (tf32) operands
+constexpr uint32_t kLayoutSW128 = 2, kLayoutSW128Atom32 = 1;
+__device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint32_t sbo,
+                                              uint32_t layout) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version for tcgen05
+  d |= (uint64_t)layout << 61;
+  return d;
+}
+// K-major tile: rows of 128 B (32 tf32 along K), 8-row groups 1024 B apart;
+// one 8-deep k-step is a 32-byte advance inside the swizzled row.
+__device__ __forceinline__ uint64_t kmajor_desc(uint32_t tile, int k) {
+  return smem_desc(tile + 32 * k, 16, 1024, kLayoutSW128);
+}
+// MN-major tile: 32-wide chunks of BK rows (128 B per K-row) 4 KB apart;
+// 4-row swizzle groups 512 B apart; one 8-deep k-step is 8 rows = 1024 B.
+__device__ __forceinline__ uint64_t mnmajor_desc(uint32_t tile, int k) {
+  return smem_desc(tile + 1024 * k, 4096, 512, kLayoutSW128Atom32);
+}
+
+// Instruction descriptor: kind::tf32, fp32 accumulate, M=128, N=BN.
+template <int A_MN, int B_MN>
+__host__ __device__ constexpr uint32_t idesc_tf32() {
+  return (1u << 4)                 // D format: f32
+         | (2u << 7)               // A format: tf32
+         | (2u << 10)              // B format: tf32
+         | ((uint32_t)A_MN << 15)  // A major (1 = MN)
+         | ((uint32_t)B_MN << 16)  // B major (1 = MN)
+         | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+struct Params {
+  int M, N, K;
+  float* C;
+  int64_t ldc;
+  const float* bias;
+  int accumulate;
+  int epilogue;
+};
+
+// TA: 0 = A stored [M][K] (K-major), 1 = A stored [K][M] (MN-major)
+// TB: 0 = B stored [K][N] (MN-major), 1 = B stored [N][K] (K-major)
+//
+// The tensor core's fp32 accumulator rounds its additions toward zero, so a
+// long K run accumulated in one TMEM accumulator drifts (a relative bias of
+// ~1e-5 at K=4096, growing with K).  The MMAs therefore accumulate chunks of
+// KC k-blocks, alternately into two TMEM accumulators, and the epilogue warps
+// add each finished chunk into fp32 registers with round-to-nearest while
+// the tensor core fills the other accumulator.
+template <int TA, int TB>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
+                   const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBlo,
+                   Params p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = bars;                  // [STAGES] TMA -> MMA
+  uint64_t* empty = bars + STAGES;        // [STAGES] MMA -> TMA
+  uint64_t* acc_full = bars + 2 * STAGES; // [2] MMA -> epilogue (chunk finished)
+  uint64_t* acc_free = acc_full + 2;      // [2] epilogue -> MMA (chunk drained)
+  uint32_t* tmem_slot = (uint32_t*)(acc_free + 2);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.y * BM, n0 = blockIdx.x * BN;
+  const int nk = (p.K + BK - 1) / BK;
+  const int nchunks = (nk + KC - 1) / KC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_free[b]), EPI_WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  __syncthreads();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES;
+        const uint32_t ph = (kb / STAGES) & 1;
+        if (kb >= STAGES && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) break;
+        unsigned char* st = smem + s * STAGE_BYTES;
+        const uint32_t sA = smem_u32(st), sAl = sA + A_TILE;
+        const uint32_t sB = sAl + A_TILE, sBl = sB + B_TILE;
+        const uint32_t fb = smem_u32(&full[s]);
+        mbar_expect_tx(fb, STAGE_BYTES);
+        const int k0 = kb * BK;
+        if (TA == 0) {
+          tma_load_2d(sA, &tmA, fb, k0, m0);
+          tma_load_2d(sAl, &tmAlo, fb, k0, m0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BM / 32; ++c) {
+            tma_load_2d(sA + c * 4096, &tmA, fb, m0 + 32 * c, k0);
+            tma_load_2d(sAl + c * 4096, &tmAlo, fb, m0 + 32 * c, k0);
+          }
+        }
+        if (TB == 1) {
+          tma_load_2d(sB, &tmB, fb, k0, n0);
+          tma_load_2d(sBl, &tmBlo, fb, k0, n0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BN / 32; ++c) {
+            tma_load_2d(sB + c * 4096, &tmB, fb, n0 + 32 * c, k0);
+            tma_load_2d(sBl + c * 4096, &tmBlo, fb, n0 + 32 * c, k0);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_tf32<TA, TB ? 0 : 1>();
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int b = c & 1;
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        if (c >= 2 && !mbar_wait(smem_u32(&acc_free[b]), ((c >> 1) - 1) & 1)) break;
+        fence_after();
+        const int kb_end = min(nk, (c + 1) * KC);
+        for (int kb = c * KC; kb < kb_end; ++kb) {
+          const int s = kb % STAGES;
+          const uint32_t ph = (kb / STAGES) & 1;
+          if (!mbar_wait(smem_u32(&full[s]), ph)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          unsigned char* st = smem + s * STAGE_BYTES;
+          const uint32_t sA = smem_u32(st), sAl = sA + A_TILE;
+          const uint32_t sB = sAl + A_TILE, sBl = sB + B_TILE;
+#pragma unroll
+          for (int k = 0; k < BK / 8; ++k) {
+            const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+            const uint64_t al = TA ? mnmajor_desc(sAl, k) : kmajor_desc(sAl, k);
+            const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+            const uint64_t bl = TB ? kmajor_desc(sBl, k) : mnmajor_desc(sBl, k);
+            const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+            mma_tf32(acc, a, bh, idesc, first);
+            mma_tf32(acc, a, bl, idesc, 1u);
+            mma_tf32(acc, al, bh, idesc, 1u);
+          }
+          mma_commit(smem_u32(&empty[s]));  // frees the stage when these MMAs finish
+        }
+        mma_commit(smem_u32(&acc_full[b]));  // chunk ready for the epilogue
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int e = warp - 2;                    // 0..EPI_WARPS-1
+    const int quarter = warp & 3;              // TMEM lanes this warp may access
+    const int half = e >= 4 ? 1 : 0;           // which BN/2 columns it owns
+    const int row = m0 + quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    float sum[BN / 2];
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) sum[j] = 0.f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      if (!mbar_wait(smem_u32(&acc_full[b]), (c >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      __syncwarp();
+      const uint32_t base = tmem + lane_base + (uint32_t)(b * BN + half * (BN / 2));
+#pragma unroll
+      for (int q = 0; q < BN / 64; ++q) {
+        float v[32];
+        tmem_ld32(base + q * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[q * 32 + j] = __fadd_rn(sum[q * 32 + j], v[j]);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[b])) : "memory");
+    }
+    const int nb0 = n0 + half * (BN / 2);
+    if (ok && row < p.M && nb0 < p.N) {
+      if (p.bias) {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
+      }
+      if (p.epilogue == TL_EPI_RELU) {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
+      }
+      float* crow = p.C + (int64_t)row * p.ldc + nb0;
+      const bool vec_ok = (p.ldc % 4 == 0) && (((uintptr_t)p.C & 15) == 0) && nb0 + BN / 2 <= p.N;
+      if (vec_ok) {
+        float4* c4 = reinterpret_cast<float4*>(crow);
+#pragma unroll
+        for (int j = 0; j < BN / 8; ++j) {
+          float4 o = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+          if (p.accumulate) {
+            float4 q = c4[j];
+            o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
+          }
+          c4[j] = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb0 + j < p.N) crow[j] = p.accumulate ? crow[j] + sum[j] : sum[j];
+      }
+    }
+  }
+  fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+
+// hi = rna_tf32(x), lo = rna_tf32(x - hi): both exactly representable in
+// TF32, so the product does not depend on how the tensor core narrows fp32.
+__global__ void __launch_bounds__(256) split_hilo_kernel(const float* __restrict__ src,
+                                                         float* __restrict__ hi,
+                                                         float* __restrict__ lo, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float x = src[i];
+    float h = tf32_rna(x);
+    hi[i] = h;
+    lo[i] = tf32_rna(x - h);
+  }
+}
+
+// lo = x - trunc_tf32(x), exact in fp32
+__global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__ src,
+                                                       float* __restrict__ dst, int64_t n) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t n4 = n >> 2;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += stride) {
+    float4 x = ld_stream4(src + 4 * i);
+    float4 y;
+    y.x = x.x - __uint_as_float(__float_as_uint(x.x) & 0xFFFFE000u);
+    y.y = x.y - __uint_as_float(__float_as_uint(x.y) & 0xFFFFE000u);
+    y.z = x.z - __uint_as_float(__float_as_uint(x.z) & 0xFFFFE000u);
+    y.w = x.w - __uint_as_float(__float_as_uint(x.w) & 0xFFFFE000u);
+    reinterpret_cast<float4*>(dst)[i] = y;
+  }
+  for (int64_t i = 4 * n4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    dst[i] = src[i] - __uint_as_float(__float_as_uint(src[i]) & 0xFFFFE000u);
+}
+
+// ------------------------------------------------------------- host side ---
+typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                    const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                    CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+PFN_encodeTiled g_encode = nullptr;
+std::once_flag g_encode_once;
+std::mutex g_ws_mu;
+struct Workspace {
+  float* ptr = nullptr;
+  size_t floats = 0;
+};
+Workspace g_ws[64];
+std::vector<float*> g_retired;  // kept alive: captured graphs may still point at them
+
+bool load_encode() {
+  std::call_once(g_encode_once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = (PFN_encodeTiled)fn;
+  });
+  return g_encode != nullptr;
+}
+
+// 2-D fp32 tensor map over a row-major [rows][cols] matrix with leading dim ld.
+// K-major tiles use the 128-byte swizzle; MN-major tiles its 32-byte-atom form.
+bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int64_t ld,
+              uint32_t box_inner, uint32_t box_outer, bool mn_major) {
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  mn_major ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Split workspace, grown on demand outside stream capture and never freed
+// (graphs captured earlier may still reference an older buffer).
+int workspace(size_t floats, float** out, cudaStream_t st) {
+  int dev = 0;
+  TL_CUDA_TRY(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= 64) return TL_ERR_INVALID_ARG;
+  std::lock_guard<std::mutex> lk(g_ws_mu);
+  Workspace& w = g_ws[dev];
+  if (w.floats < floats) {
+    cudaStreamCaptureStatus cs;
+    if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
+      return TL_ERR_UNSUPPORTED;
+    size_t want = floats + floats / 4;
+    float* p = nullptr;
+    TL_CUDA_TRY(cudaMalloc(&p, want * 4));
+    if (w.ptr) g_retired.push_back(w.ptr);
+    w.ptr = p;
+    w.floats = want;
+  }
+  *out = w.ptr;
+  return TL_OK;
+}
+
+int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both rounded
+
+unsigned split_grid(size_t n) {
+  unsigned g = (unsigned)((n / 4 + 255) / 256);
+  unsigned cap = 8u * sm_count();
+  return g < 1 ? 1 : (g < cap ? g : cap);
+}
+
+template <int TA, int TB>
+int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
+           float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, cudaStream_t st) {
+  if (!load_encode()) return TL_ERR_UNSUPPORTED;
+  const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
+  const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
+  // the elements a row-major [rows][cols] matrix with leading dim ld spans
+  const size_t a_n = (size_t)(a_rows - 1) * lda + a_cols;
+  const size_t b_n = (size_t)(b_rows - 1) * ldb + b_cols;
+  const size_t a_pad = (a_n + 63) / 64 * 64, b_pad = (b_n + 63) / 64 * 64;
+  const bool explicit_hi = g_split_mode == 1;
+  float* ws = nullptr;
+  TL_TRY(workspace((explicit_hi ? 2 : 1) * (a_pad + b_pad), &ws, st));
+  const float *a_hi = A, *b_hi = B;
+  float *a_lo, *b_lo;
+  if (explicit_hi) {
+    float* ah = ws;
+    a_lo = ws + a_pad;
+    float* bh = a_lo + a_pad;
+    b_lo = bh + b_pad;
+    split_hilo_kernel<<<split_grid(a_n), 256, 0, st>>>(A, ah, a_lo, (int64_t)a_n);
+    TL_TRY(after_launch());
+    split_hilo_kernel<<<split_grid(b_n), 256, 0, st>>>(B, bh, b_lo, (int64_t)b_n);
+    TL_TRY(after_launch());
+    a_hi = ah;
+    b_hi = bh;
+  } else {
+    a_lo = ws;
+    b_lo = ws + a_pad;
+    split_lo_kernel<<<split_grid(a_n), 256, 0, st>>>(A, a_lo, (int64_t)a_n);
+    TL_TRY(after_launch());
+    split_lo_kernel<<<split_grid(b_n), 256, 0, st>>>(B, b_lo, (int64_t)b_n);
+    TL_TRY(after_launch());
+  }
+
+  CUtensorMap ma, mal, mb, mbl;
+  const uint32_t a_inner = 32, a_outer = TA ? 32 : BM;
+  const uint32_t b_inner = 32, b_outer = TB ? BN : 32;
+  const bool a_mn = TA == 1, b_mn = TB == 0;
+  if (!make_map(&ma, a_hi, a_rows, a_cols, lda, a_inner, a_outer, a_mn) ||
+      !make_map(&mal, a_lo, a_rows, a_cols, lda, a_inner, a_outer, a_mn) ||
+      !make_map(&mb, b_hi, b_rows, b_cols, ldb, b_inner, b_outer, b_mn) ||
+      !make_map(&mbl, b_lo, b_rows, b_cols, ldb, b_inner, b_outer, b_mn))
+    return TL_ERR_UNSUPPORTED;
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
+  auto kern = gemm_tc_kernel<TA, TB>;
+  TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mal, mb, mbl, p);
+  return after_launch();
+}
+
+}  // namespace
+
+bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                const float* B, int64_t ldb, const float* C, int64_t ldc) {
+  (void)C;
+  (void)ldc;
+  if (!load_encode()) return false;
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (major != 10) return false;
+  if (M < 64 || N < 32 || K < 32) return false;          // small products: CUDA cores
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  if (lda % 4 || ldb % 4) return false;                  // TMA strides: multiples of 16 B
+  if (((uintptr_t)A & 15) || ((uintptr_t)B & 15)) return false;
+  const int64_t a_cols = ta ? M : K, b_cols = tb ? K : N;
+  if (lda < a_cols || ldb < b_cols) return false;
+  return true;
+}
+
+int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+            const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
+            int epilogue, cudaStream_t st) {
+  if (!ta && !tb) return launch<0, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+  if (!ta && tb) return launch<0, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+  if (ta && !tb) return launch<1, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+  return launch<1, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+}
+
+void gemm_set_split_mode(int mode) { g_split_mode = mode; }
+
 }  // namespace tl
+
+extern "C" int tl_device_error(int* code, int reset) {
+  int v = 0;
+  TL_CUDA_TRY(cudaMemcpyFromSymbol(&v, tl::g_device_error, sizeof(int)));
+  if (code) *code = v;
+  if (reset && v) {
+    int z = 0;
+    TL_CUDA_TRY(cudaMemcpyToSymbol(tl::g_device_error, &z, sizeof(int)));
+  }
+  return TL_OK;
+}

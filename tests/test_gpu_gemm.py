@@ -1,0 +1,97 @@
+"""tl_gemm on the GPU against a float64 product.
+
+Covers every storage combination the executor uses (A as stored or
+transposed, B as stored or transposed), ragged M/N/K (the tensor-core tiles
+are 128x256x32, so partial tiles exercise TMA zero fill and masked stores),
+bias, relu and accumulate.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
+the split-TF32 product is expected near 1e-6.  Also checks which path a
+shape takes and that no kernel left a device error.
+"""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import assert_close, load_backend
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(64, 32, 32), (128, 256, 64), (200, 300, 100), (1024, 512, 512), (332, 1000, 780),
+          (4096, 256, 4096), (256, 128, 16384)]
+
+
+def _run(ta, tb, M, N, K, bias=False, acc=False, relu=False, seed=0):
+    tl = load_backend()
+    rt = tl.runtime
+    L = rt.lib()
+    dev = rt.Device.get(0)
+    rng = np.random.default_rng(seed + M + N + K + 7 * ta + 3 * tb)
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    bv = rng.standard_normal(N).astype(np.float32)
+    dA, dB, dC, db = (rt.DeviceBuffer(dev, a.shape) for a in (A, B, C0, bv))
+    dA.upload(A)
+    dB.upload(B)
+    dC.upload(C0)
+    db.upload(bv)
+    lda, ldb = A.shape[1], B.shape[1]
+    path = L.tl_gemm_path(ta, tb, M, N, K, dA.ptr, lda, dB.ptr, ldb, dC.ptr, N)
+    rt.check(L.tl_gemm(ta, tb, M, N, K, dA.ptr, lda, dB.ptr, ldb, dC.ptr, N,
+                       db.ptr if bias else None, 1 if acc else 0, 1 if relu else 0, dev.stream))
+    out = dC.download()
+    err = ctypes.c_int(0)
+    rt.check(L.tl_device_error(ctypes.byref(err), 1))
+    Am = A.astype(np.float64).T if ta else A.astype(np.float64)
+    Bm = B.astype(np.float64).T if tb else B.astype(np.float64)
+    ref = Am @ Bm
+    if bias:
+        ref = ref + bv
+    if relu:
+        ref = np.maximum(ref, 0)
+    if acc:
+        ref = ref + C0
+    for b in (dA, dB, dC, db):
+        b.free()
+    return out, ref, path, err.value
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_layouts(ta, tb, M, N, K):
+    out, ref, path, err = _run(ta, tb, M, N, K)
+    assert err == 0
+    assert path == 0, "this shape should run on the tensor cores"
+    # split-TF32 keeps fp32-level accuracy: far inside the 1e-4 bar
+    assert_close(out, ref, 1e-5, f"gemm ta={ta} tb={tb} {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("bias,acc,relu", [(True, False, False), (False, True, False),
+                                           (True, False, True), (True, True, False)])
+def test_gemm_epilogues(bias, acc, relu):
+    out, ref, path, err = _run(0, 0, 300, 520, 200, bias=bias, acc=acc, relu=relu)
+    assert err == 0 and path == 0
+    assert_close(out, ref, 1e-5, "epilogue")
+
+
+@pytest.mark.parametrize("M,N,K", [(64, 10, 4096), (10, 64, 100), (7, 5, 3), (4096, 10, 64),
+                                   (333, 1000, 777)])
+def test_gemm_cuda_core_shapes(M, N, K):
+    # leading dimensions that are not a multiple of 4 floats (16 bytes), or
+    # products too small or too narrow for 128x256 tiles, take the CUDA cores
+    out, ref, path, err = _run(0, 0, M, N, K, bias=True)
+    assert path == 1
+    assert_close(out, ref, 1e-5, "cuda-core gemm")
+
+
+def test_gemm_explicit_split_mode():
+    tl = load_backend()
+    L = tl.runtime.lib()
+    L.tl_gemm_force_simt(2)
+    try:
+        for ta, tb in [(0, 0), (1, 1)]:
+            out, ref, path, err = _run(ta, tb, 520, 264, 300)
+            assert err == 0 and path == 0
+            assert_close(out, ref, 1e-5, "explicit split")
+    finally:
+        L.tl_gemm_force_simt(0)
