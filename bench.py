@@ -319,6 +319,62 @@ def run_ours(args, rank, world, local):
     return 0
 
 
+def run_micro(args):
+    """One kernel alone, for profiling and per-kernel rooflines:
+    gemm     65536/8 x 4096 x 4096 linear forward (A 128 MiB, B 64 MiB)
+    fused    the [8192,8192] fused elementwise chain
+    softmax  softmax over rows of [16384,4096]
+    rowsum   sum over rows of [16384,4096]
+    """
+    from __graft_entry__ import load_package
+    tl = load_package()
+    rt = tl.runtime
+    L = rt.lib()
+    dev = rt.Device.get(0)
+    st = dev.stream
+    hbm, bf16, _, src = peaks()
+    reps = args.steps
+    if args.micro == "gemm":
+        M, N, K = 8192, 4096, 4096
+        rng = np.random.default_rng(0)
+        A = rt.DeviceBuffer(dev, (M, K))
+        A.upload(rng.standard_normal((M, K), dtype=np.float32))
+        B = rt.DeviceBuffer(dev, (K, N))
+        B.upload((rng.standard_normal((K, N), dtype=np.float32) / 64).astype(np.float32))
+        C = rt.DeviceBuffer(dev, (M, N))
+        bias = rt.DeviceBuffer(dev, (N,), zero=True)
+        fn = lambda: rt.check(L.tl_gemm(0, 0, M, N, K, A.ptr, K, B.ptr, N, C.ptr, N, bias.ptr, 0, 0, st))  # noqa: E731
+        work, unit, peak = 2.0 * M * N * K, "TFLOP/s", bf16
+    elif args.micro == "fused":
+        pr = tl.programs
+        P = tl.Program(pr.fused_chain(FUSED_N), None, feeds=pr.fused_chain_inputs(FUSED_N), fetch=["y", "m"])
+        P.prepare()
+        fn = P.execute
+        work, unit, peak = float(FUSED_BYTES), "GB/s", hbm
+    else:
+        R, C_ = 16384, 4096
+        x = rt.DeviceBuffer(dev, (R, C_))
+        x.upload(np.random.default_rng(1).standard_normal((R, C_), dtype=np.float32))
+        y = rt.DeviceBuffer(dev, (R, C_) if args.micro == "softmax" else (R,))
+        if args.micro == "softmax":
+            fn = lambda: rt.check(L.tl_softmax_rows(x.ptr, y.ptr, R, C_, st))  # noqa: E731
+            work = 8.0 * R * C_
+        else:
+            fn = lambda: rt.check(L.tl_reduce_rows(0, x.ptr, y.ptr, R, C_, st))  # noqa: E731
+            work = 4.0 * R * C_ + 4.0 * R
+        unit, peak = "GB/s", hbm
+    for _ in range(max(3, args.warmup)):
+        fn()
+    dev.sync()
+    ms = time_events(tl, st, fn, reps)
+    scale = 1e12 if unit == "TFLOP/s" else 1e9
+    ach = work / (ms * 1e-3) / scale
+    print(json.dumps({"micro": args.micro, "ms_per_launch": ms, "achieved": ach, "unit": unit,
+                      "peak": peak, "frac": ach / peak, "peak_source": src, "launches": reps}),
+          flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -328,7 +384,11 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fused", action="store_true")
+    ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum"], default=None,
+                    help="time one kernel alone (profiling aid); prints its own JSON line")
     args = ap.parse_args()
+    if args.micro:
+        return run_micro(args)
     rank, world, local = dist_env()
     if args.impl == "reference":
         return run_reference(args, rank, world)
