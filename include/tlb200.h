@@ -206,8 +206,9 @@ int  tl_concat_rows(const float* a, const float* b, float* out, int64_t rows_a,
  * elements of the row-major storage.  f32 in, f32 out.  On sm_100a the
  * product runs on tcgen05 tensor cores as split-TF32 (three TF32 products
  * hi*hi + hi*lo + lo*hi with fp32 accumulation in tensor memory), which
- * keeps fp32-level accuracy; shapes the TMA path cannot describe take a
- * tiled fp32 CUDA-core path.
+ * keeps fp32-level accuracy; skinny products (N <= 32, or K <= 32 with B
+ * transposed) take bandwidth-bound CUDA-core kernels; other shapes the TMA
+ * path cannot describe take a tiled fp32 CUDA-core path.
  * epilogue: 0 none, 1 relu (y = max(0, y)).
  * accumulate: 0 overwrite C, 1 C += result.
  */

@@ -20,6 +20,10 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
 bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                 const float* B, int64_t ldb, const float* C, int64_t ldc);
 void gemm_set_split_mode(int mode);
+int gemm_small(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+               const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
+               int accumulate, int epilogue, cudaStream_t st);
+bool gemm_small_ok(int ta, int tb, int64_t M, int64_t N, int64_t K);
 
 namespace {
 
@@ -158,6 +162,11 @@ int tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const flo
   if (!tl::g_force_simt && tl::gemm_tc_ok(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc))
     return tl::gemm_tc(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
                        epilogue, st);
+  if (K > 0 && tl::gemm_small_ok(trans_a, trans_b, M, N, K)) {
+    int s = tl::gemm_small(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
+                           epilogue, st);
+    if (s != TL_ERR_UNSUPPORTED) return s;
+  }
   return tl::gemm_simt(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
                        epilogue, st);
 }

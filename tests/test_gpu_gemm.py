@@ -74,14 +74,24 @@ def test_gemm_epilogues(bias, acc, relu):
     assert_close(out, ref, 1e-5, "epilogue")
 
 
-@pytest.mark.parametrize("M,N,K", [(64, 10, 4096), (10, 64, 100), (7, 5, 3), (4096, 10, 64),
-                                   (333, 1000, 777)])
+@pytest.mark.parametrize("M,N,K", [(10, 64, 100), (7, 5, 3), (333, 1000, 777), (3, 6, 4)])
 def test_gemm_cuda_core_shapes(M, N, K):
     # leading dimensions that are not a multiple of 4 floats (16 bytes), or
     # products too small or too narrow for 128x256 tiles, take the CUDA cores
     out, ref, path, err = _run(0, 0, M, N, K, bias=True)
     assert path == 1
     assert_close(out, ref, 1e-5, "cuda-core gemm")
+
+
+@pytest.mark.parametrize("ta,tb,M,N,K", [(0, 0, 8192, 10, 4096), (1, 0, 2048, 10, 16384),
+                                         (1, 0, 333, 7, 5000), (0, 1, 8192, 1024, 10),
+                                         (0, 1, 70000, 40, 3), (0, 0, 16, 10, 4096)])
+@pytest.mark.parametrize("bias,acc", [(True, False), (False, True)])
+def test_gemm_skinny(ta, tb, M, N, K, bias, acc):
+    """Classifier-head products (N or K of 10) on the bandwidth-bound kernels."""
+    out, ref, path, err = _run(ta, tb, M, N, K, bias=bias, acc=acc)
+    assert path == 1
+    assert_close(out, ref, 1e-5, f"skinny {ta}{tb} {M}x{N}x{K}")
 
 
 def test_gemm_explicit_split_mode():
