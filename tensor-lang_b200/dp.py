@@ -176,12 +176,16 @@ class AllReduce(Step):
     def bind(self, P):
         L = rt.lib()
         spans = []
-        for n in self.names:
-            p, cnt = P.ptr(n), numel(P.shapes[n])
-            if spans and spans[-1][0] + 4 * spans[-1][1] == p:
-                spans[-1][1] += cnt
-            else:
-                spans.append([p, cnt])
+        arena = P.arena_span()
+        if arena is not None and set(self.names) <= set(P.arena_names):
+            spans.append(list(arena))  # one call over the packed arena
+        else:
+            for n in self.names:
+                p, cnt = P.ptr(n), numel(P.shapes[n])
+                if spans and spans[-1][0] + 4 * spans[-1][1] == p:
+                    spans[-1][1] += cnt
+                else:
+                    spans.append([p, cnt])
         h, stream = self.comm.handle, P.stream
 
         def run():

@@ -477,12 +477,15 @@ class Program:
                 b = self.alias.get(n, n)
                 if b not in bases:
                     bases.append(b)
-            total = sum(numel(self.shapes[b]) for b in bases)
-            self._arena = rt.DeviceBuffer(self.dev, (total,))
+            # 64-float (256-byte) aligned slots: every tensor keeps the
+            # alignment TMA and vector loads need; the padding is all-reduced too
+            pad = lambda n: (n + 63) // 64 * 64  # noqa: E731
+            total = sum(pad(numel(self.shapes[b])) for b in bases)
+            self._arena = rt.DeviceBuffer(self.dev, (total,), zero=True)
             off = 0
             for b in bases:
                 self.buffers[b] = rt.DeviceBuffer.view(self._arena, off, self.shapes[b])
-                off += numel(self.shapes[b])
+                off += pad(numel(self.shapes[b]))
         for n in sorted(needed):
             base = self.alias.get(n, n)
             if base in self.buffers:
@@ -558,6 +561,11 @@ class Program:
                 p.parent.mkdir(parents=True, exist_ok=True)
                 np.save(p, self.read(sv["tensor"]))
         return out
+
+    def arena_span(self):
+        """(pointer, float count) of the packed gradient arena, or None."""
+        a = getattr(self, "_arena", None)
+        return (a.ptr, a.size) if a is not None else None
 
     @property
     def loops(self) -> List[_Loop]:

@@ -1,0 +1,136 @@
+"""Host-side logic of the data-parallel path, on CPU with 2 processes.
+
+* the TCP rendezvous (broadcast, gather, barrier) between 2 ranks, and its
+  failure detection: a rank that never arrives makes the other fail within
+  the timeout instead of hanging;
+* batch sharding: which tensors carry the batch axis, their per-rank shapes,
+  and the global divisors of the loss VJPs;
+* the identity the design rests on, with torch.distributed (gloo): each rank
+  computes its shard's gradients with the global-batch divisor, the
+  all-reduced sum equals the full-batch gradient (float64 oracle).
+"""
+import multiprocessing as mp
+import os
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import load_backend
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _rdv_worker(rank, world, port, q):
+    tl = load_backend()
+    from tensor_lang_b200 import dp
+    r = dp.Rendezvous(rank, world, "127.0.0.1", port, timeout=20)
+    got = r.bcast({"from": 0, "v": [1, 2, 3]} if rank == 0 else None)
+    g = r.gather(rank * 10)
+    r.barrier()
+    q.put((rank, got, g))
+    r.close()
+
+
+def test_rendezvous_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_rdv_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (got, g)) for r, got, g in (q.get(timeout=60) for _ in ps))
+    for p in ps:
+        p.join(timeout=30)
+        assert p.exitcode == 0
+    assert res[0][0] == res[1][0] == {"from": 0, "v": [1, 2, 3]}
+    assert res[0][1] == [0, 10] and res[1][1] is None
+
+
+def _lonely_root(port, q):
+    load_backend()
+    from tensor_lang_b200 import dp
+    try:
+        dp.Rendezvous(0, 2, "127.0.0.1", port, timeout=2)
+        q.put("no error")
+    except (TimeoutError, socket.timeout, OSError) as e:
+        q.put(type(e).__name__)
+
+
+def test_rendezvous_missing_rank_times_out():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    p = ctx.Process(target=_lonely_root, args=(_free_port(), q))
+    p.start()
+    res = q.get(timeout=60)
+    p.join(timeout=30)
+    assert res != "no error"
+
+
+def test_sharding_and_divisors():
+    tl = load_backend()
+    from tensor_lang_b200 import dp
+    from tensor_lang_b200.shapes import complete_env
+    ast = tl.programs.mlp3_train(B=1024, I=32, H=64, C=10, epochs=2)
+    derived = dp.batch_derived(ast, ["x", "t"])
+    assert {"x", "t", "h1", "a1", "h2", "a2", "z", "p"} <= derived
+    assert not derived & {"W1", "b1", "W2", "b2", "W3", "b3", "loss", "W1_new", "b3_step"}
+    g = complete_env(ast, {})
+    local = dp.shard_shapes(g, derived, 4)
+    assert local["x"] == (256, 32) and local["h2"] == (256, 64) and local["h2_grad"] == (256, 64)
+    assert local["W2"] == (64, 64) and local["W2_grad"] == (64, 64)
+    assert dp.loss_divisors(ast, g, derived) == {("ce", "loss"): 1024.0}
+    with pytest.raises(ValueError):
+        dp.shard_shapes(g, derived, 3)
+
+
+def _grad_worker(rank, world, port, q):
+    import torch
+    import torch.distributed as dist
+    from oracle import OracleProgram
+    tl = load_backend()
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    kw = dict(B=64, I=16, H=32, C=10)
+    B, b = kw["B"], kw["B"] // world
+    ast = tl.programs.mlp2_step(B=b, I=kw["I"], H=kw["H"], C=kw["C"])
+    full = tl.programs.mlp2_inputs(B=B, I=kw["I"], H=kw["H"], C=kw["C"], seed=9)
+    feeds = dict(full, x=full["x"][rank * b:(rank + 1) * b], t=full["t"][rank * b:(rank + 1) * b])
+    env = {k: {"shape": v} for k, v in tl.shapes.complete_env(ast, {}).items()}
+    out = OracleProgram(ast, env, dtype=np.float64, feeds=feeds).run()
+    names = ["W1_grad", "b1_grad", "W2_grad", "b2_grad"]
+    # the shard's CE VJP divided by b; the global divisor is B
+    mine = {n: torch.tensor(out[n] * (b / B)) for n in names}
+    for n in names:
+        dist.all_reduce(mine[n])
+    q.put((rank, {n: mine[n].numpy() for n in names}))
+    dist.destroy_process_group()
+
+
+def test_sharded_gradient_sum_equals_full_batch():
+    from oracle import OracleProgram
+    tl = load_backend()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    ps = [ctx.Process(target=_grad_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    kw = dict(B=64, I=16, H=32, C=10)
+    ast = tl.programs.mlp2_step(**kw)
+    feeds = tl.programs.mlp2_inputs(seed=9, **kw)
+    env = {k: {"shape": v} for k, v in tl.shapes.complete_env(ast, {}).items()}
+    ref = OracleProgram(ast, env, dtype=np.float64, feeds=feeds).run()
+    for n, v in res[0].items():
+        np.testing.assert_allclose(v, ref[n], rtol=1e-10, atol=1e-12, err_msg=n)
+        np.testing.assert_array_equal(v, res[1][n])
