@@ -101,6 +101,105 @@ __global__ void __launch_bounds__(256) softmax_rows_block(const float* __restric
   }
 }
 
+// Register-resident rows: 128 threads per row, each holding VPT float4s
+// (rows up to 512*VPT wide, a multiple of 4).  One HBM read and one write per
+// element, no shared-memory staging, two block reductions per row.
+constexpr int RT = 128;  // threads per row
+
+__device__ __forceinline__ float block128_max(float v, float* sh) {
+  v = warp_max(v);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  v = fmaxf(fmaxf(sh[0], sh[1]), fmaxf(sh[2], sh[3]));
+  return v;
+}
+__device__ __forceinline__ double block128_sum(double v, double* sh) {
+  v = warp_sum(v);
+  if ((threadIdx.x & 31) == 0) sh[threadIdx.x >> 5] = v;
+  __syncthreads();
+  return (sh[0] + sh[1]) + (sh[2] + sh[3]);
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(RT) softmax_rows_reg(const float* __restrict__ in,
+                                                       float* __restrict__ out, int64_t cols) {
+  __shared__ float shm[4];
+  __shared__ double shd[4];
+  const float* p = in + (int64_t)blockIdx.x * cols;
+  const int n4 = (int)(cols >> 2);
+  float4 x[VPT];
+  float m = -INFINITY;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    x[v] = i < n4 ? ld_stream4(p + 4 * i) : make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY);
+    m = fmaxf(fmaxf(fmaxf(m, x[v].x), fmaxf(x[v].y, x[v].z)), x[v].w);
+  }
+  m = block128_max(m, shm);
+  double s = 0.0;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    if (i < n4) {
+      x[v].x = expf(x[v].x - m); x[v].y = expf(x[v].y - m);
+      x[v].z = expf(x[v].z - m); x[v].w = expf(x[v].w - m);
+      s += (double)((x[v].x + x[v].y) + (x[v].z + x[v].w));
+    }
+  }
+  const float tot = (float)block128_sum(s, shd);
+  float* q = out + (int64_t)blockIdx.x * cols;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    if (i < n4)
+      st_stream4(q + 4 * i, make_float4(x[v].x / tot, x[v].y / tot, x[v].z / tot, x[v].w / tot));
+  }
+}
+
+template <int VPT>
+__global__ void __launch_bounds__(RT) layer_norm_rows_reg(const float* __restrict__ in,
+                                                          float* __restrict__ out, int64_t cols,
+                                                          float eps) {
+  __shared__ double shd[2][4];
+  const float* p = in + (int64_t)blockIdx.x * cols;
+  const int n4 = (int)(cols >> 2);
+  float4 x[VPT];
+  double s = 0.0;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    x[v] = i < n4 ? ld_stream4(p + 4 * i) : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += (double)x[v].x; s += (double)x[v].y; s += (double)x[v].z; s += (double)x[v].w;
+  }
+  const float mean = (float)(block128_sum(s, shd[0]) / (double)cols);
+  double ss = 0.0;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    if (i < n4) {
+      x[v].x -= mean; x[v].y -= mean; x[v].z -= mean; x[v].w -= mean;
+      ss += (double)x[v].x * x[v].x; ss += (double)x[v].y * x[v].y;
+      ss += (double)x[v].z * x[v].z; ss += (double)x[v].w * x[v].w;
+    }
+  }
+  const float var = (float)(block128_sum(ss, shd[1]) / (double)cols);
+  const float sd = sqrtf(var + eps);
+  float* q = out + (int64_t)blockIdx.x * cols;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = threadIdx.x + v * RT;
+    if (i < n4) st_stream4(q + 4 * i, make_float4(x[v].x / sd, x[v].y / sd, x[v].z / sd, x[v].w / sd));
+  }
+}
+
+// VPT choice for a row of `cols` floats (cols % 4 == 0): 0 when too wide
+int rows_vpt(int64_t cols) {
+  const int64_t n4 = cols / 4;
+  for (int v : {1, 2, 4, 8, 16})
+    if (n4 <= (int64_t)v * RT) return v;
+  return 0;
+}
+
 // Rows too wide for shared memory: three passes over global memory.
 __global__ void __launch_bounds__(256) softmax_rows_global(const float* __restrict__ in,
                                                            float* __restrict__ out, int64_t cols) {
@@ -454,8 +553,17 @@ extern "C" {
 int tl_softmax_rows(const float* in, float* out, int64_t rows, int64_t cols, void* stream) {
   if (!in || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARG;
   cudaStream_t st = tl::stream_or_default(stream);
+  const int vpt = (cols % 4 == 0 && tl::aligned16(in) && tl::aligned16(out)) ? tl::rows_vpt(cols) : 0;
   if (cols <= tl::kWarpCols) {
     tl::softmax_rows_warp<<<tl::ceil_div_u(rows, 8), 256, 0, st>>>(in, out, rows, (int)cols);
+  } else if (vpt && rows <= INT32_MAX) {
+    switch (vpt) {
+      case 1: tl::softmax_rows_reg<1><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols); break;
+      case 2: tl::softmax_rows_reg<2><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols); break;
+      case 4: tl::softmax_rows_reg<4><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols); break;
+      case 8: tl::softmax_rows_reg<8><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols); break;
+      default: tl::softmax_rows_reg<16><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols); break;
+    }
   } else if (cols <= tl::kSmemRowMax) {
     size_t smem = (size_t)cols * 4;
     if (smem > 48 * 1024)
@@ -483,8 +591,17 @@ int tl_layer_norm_rows(const float* in, float* out, int64_t rows, int64_t cols, 
                        void* stream) {
   if (!in || !out || rows <= 0 || cols <= 0) return TL_ERR_INVALID_ARG;
   cudaStream_t st = tl::stream_or_default(stream);
+  const int vpt = (cols % 4 == 0 && tl::aligned16(in) && tl::aligned16(out)) ? tl::rows_vpt(cols) : 0;
   if (cols <= tl::kWarpCols) {
     tl::layer_norm_rows_warp<<<tl::ceil_div_u(rows, 8), 256, 0, st>>>(in, out, rows, (int)cols, eps);
+  } else if (vpt && rows <= INT32_MAX) {
+    switch (vpt) {
+      case 1: tl::layer_norm_rows_reg<1><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols, eps); break;
+      case 2: tl::layer_norm_rows_reg<2><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols, eps); break;
+      case 4: tl::layer_norm_rows_reg<4><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols, eps); break;
+      case 8: tl::layer_norm_rows_reg<8><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols, eps); break;
+      default: tl::layer_norm_rows_reg<16><<<(unsigned)rows, tl::RT, 0, st>>>(in, out, cols, eps); break;
+    }
   } else {
     int staged = cols <= tl::kSmemRowMax;
     size_t smem = staged ? (size_t)cols * 4 : 0;

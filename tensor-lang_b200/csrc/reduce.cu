@@ -20,6 +20,7 @@ namespace {
 
 constexpr int kAssumedSms = 148;      // planning constant for chunk counts
 constexpr int kFullMaxBlocks = 2048;  // upper bound of full-reduction blocks
+constexpr int kFullBlocksPerSm = 4;   // launch bounds keep 4 blocks of 256 resident per SM
 // Every scratch buffer starts with a fixed counter region; partials follow it,
 // so reductions of different kinds may share one scratch buffer in stream order.
 constexpr size_t kCounterBytes = 4096;
@@ -127,10 +128,17 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restric
 }
 
 // ------------------------------------------------------------ axis = 0 ----
+// A block owns a stripe of 32*VEC columns (lane l: columns 4l..4l+3 when
+// VEC = 4) and a chunk of rows; its 8 warps take every 8th row of the chunk
+// (4 rows in flight per trip) and fold their results through shared memory
+// in warp order.  Each block writes one partial per column; the last block of
+// a stripe folds the chunks' partials in chunk order.  Both folds are fixed-
+// order, so results do not depend on timing.
+constexpr int kColBlocksPerSm = 4;  // launch bounds below keep 4 resident
+
 struct ColPlan {
-  int vec;      // 4 when each thread owns a float4 column group, else 1
-  int threads;  // block size
-  unsigned gx;  // column blocks
+  int vec;      // 4: float4 per lane, else 1
+  unsigned gx;  // column stripes
   unsigned gy;  // row chunks
   int64_t chunk;
 };
@@ -138,14 +146,12 @@ struct ColPlan {
 ColPlan col_plan(int64_t rows, int64_t cols, bool vec_ok) {
   ColPlan p;
   p.vec = vec_ok ? 4 : 1;
-  p.threads = 256;
-  int64_t groups = cols / p.vec;
-  if (groups < 256) p.threads = (int)((groups + 31) / 32 * 32);
-  if (p.threads < 32) p.threads = 32;
-  p.gx = ceil_div_u(groups, p.threads);
-  int64_t want = (4LL * kAssumedSms + p.gx - 1) / p.gx;
-  int64_t maxy = rows < 1024 ? rows : 1024;
+  p.gx = ceil_div_u(cols, 32LL * p.vec);
+  // one resident wave: kColBlocksPerSm blocks of 256 threads on every SM
+  int64_t want = (kColBlocksPerSm * kAssumedSms + p.gx - 1) / p.gx;
+  int64_t maxy = (rows + 63) / 64;  // at least 64 rows per chunk
   if (want > maxy) want = maxy;
+  if (want > 256) want = 256;
   if (want < 1) want = 1;
   p.chunk = (rows + want - 1) / want;
   p.gy = (unsigned)((rows + p.chunk - 1) / p.chunk);
@@ -154,102 +160,142 @@ ColPlan col_plan(int64_t rows, int64_t cols, bool vec_ok) {
 
 size_t col_partial_bytes(int op) { return (op == TL_RED_ARGMAX || op == TL_RED_ARGMIN) ? 16 : 8; }
 
-// Column reduction with fixed-order combine.  scratch layout:
-//   [0, 4*gx) unsigned counters (padded to 256 B) | partials[gy][cols]
+template <int OP>
+struct ColAcc {
+  double s;
+  float m;
+  int64_t i;
+};
+
+template <int OP>
+__device__ __forceinline__ void col_init(ColAcc<OP>& a) {
+  a.s = 0.0;
+  a.m = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
+  a.i = INT64_MAX;
+}
+template <int OP>
+__device__ __forceinline__ void col_add(ColAcc<OP>& a, float x, int64_t r) {
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) a.s += (double)x;
+  else if constexpr (OP == TL_RED_MAX) a.m = fmaxf(a.m, x);
+  else if constexpr (OP == TL_RED_MIN) a.m = fminf(a.m, x);
+  else arg_take<OP == TL_RED_ARGMAX>(a.m, a.i, x, r);
+}
+template <int OP>
+__device__ __forceinline__ void col_merge(ColAcc<OP>& a, const ColAcc<OP>& b) {
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) a.s += b.s;
+  else if constexpr (OP == TL_RED_MAX) a.m = fmaxf(a.m, b.m);
+  else if constexpr (OP == TL_RED_MIN) a.m = fminf(a.m, b.m);
+  else if (arg_better<OP == TL_RED_ARGMAX>(b.m, b.i, a.m, a.i)) { a.m = b.m; a.i = b.i; }
+}
+template <int OP>
+__device__ __forceinline__ void col_store(void* partials, size_t off, const ColAcc<OP>& a) {
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) ((double*)partials)[off] = a.s;
+  else if constexpr (OP == TL_RED_MAX || OP == TL_RED_MIN) ((float*)partials)[2 * off] = a.m;
+  else {
+    ((float*)partials)[4 * off] = a.m;
+    ((int64_t*)partials)[2 * off + 1] = a.i;
+  }
+}
+template <int OP>
+__device__ __forceinline__ ColAcc<OP> col_load(const void* partials, size_t off) {
+  ColAcc<OP> a;
+  col_init(a);
+  if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) a.s = __ldcg(&((const double*)partials)[off]);
+  else if constexpr (OP == TL_RED_MAX || OP == TL_RED_MIN) a.m = __ldcg(&((const float*)partials)[2 * off]);
+  else {
+    a.m = __ldcg(&((const float*)partials)[4 * off]);
+    a.i = __ldcg(&((const int64_t*)partials)[2 * off + 1]);
+  }
+  return a;
+}
+
 template <int OP, int VEC>
-__global__ void __launch_bounds__(256) reduce_cols_kernel(const float* __restrict__ in,
+__global__ void __launch_bounds__(256, kColBlocksPerSm) reduce_cols_kernel(const float* __restrict__ in,
                                                           float* __restrict__ out, int64_t rows,
                                                           int64_t cols, int64_t chunk,
                                                           unsigned* counters, void* partials) {
-  constexpr bool ARG = (OP == TL_RED_ARGMAX || OP == TL_RED_ARGMIN);
-  constexpr bool L = (OP == TL_RED_ARGMAX);
-  const int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;  // column group
-  const int64_t c0 = g * VEC;
+  __shared__ ColAcc<OP> sh[8][32 * VEC];
+  __shared__ unsigned is_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t c0 = (int64_t)blockIdx.x * 32 * VEC + (int64_t)lane * VEC;
   const bool active = c0 < cols;
-  const int64_t r0 = (int64_t)blockIdx.y * chunk;
-  int64_t r1 = r0 + chunk;
-  if (r1 > rows) r1 = rows;
+  const int64_t r_begin = (int64_t)blockIdx.y * chunk;
+  const int64_t r_end = r_begin + chunk < rows ? r_begin + chunk : rows;
 
-  double s[VEC];
-  float m[VEC];
-  int64_t ix[VEC];
+  ColAcc<OP> acc[VEC];
 #pragma unroll
-  for (int k = 0; k < VEC; ++k) {
-    s[k] = 0.0;
-    m[k] = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
-    ix[k] = INT64_MAX;
-  }
+  for (int k = 0; k < VEC; ++k) col_init(acc[k]);
   if (active) {
-    for (int64_t r = r0; r < r1; ++r) {
-      float x[VEC];
+    int64_t r = r_begin + warp;
+    for (; r + 24 < r_end; r += 32) {  // 4 rows in flight per trip
+      float x[4][VEC];
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float* p = in + (r + 8 * q) * cols + c0;
+        if constexpr (VEC == 4) {
+          float4 a = ld_stream4(p);
+          x[q][0] = a.x; x[q][1] = a.y; x[q][2] = a.z; x[q][3] = a.w;
+        } else {
+          x[q][0] = *p;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+#pragma unroll
+        for (int k = 0; k < VEC; ++k) col_add(acc[k], x[q][k], r + 8 * q);
+    }
+    for (; r < r_end; r += 8) {
+      const float* p = in + r * cols + c0;
       if constexpr (VEC == 4) {
-        float4 a = ld_stream4(in + r * cols + c0);
-        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        float4 a = ld_stream4(p);
+        col_add(acc[0], a.x, r); col_add(acc[1], a.y, r); col_add(acc[2], a.z, r); col_add(acc[3], a.w, r);
       } else {
-        x[0] = in[r * cols + c0];
-      }
-#pragma unroll
-      for (int k = 0; k < VEC; ++k) {
-        if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) s[k] += (double)x[k];
-        else if constexpr (OP == TL_RED_MAX) m[k] = fmaxf(m[k], x[k]);
-        else if constexpr (OP == TL_RED_MIN) m[k] = fminf(m[k], x[k]);
-        else arg_take<L>(m[k], ix[k], x[k], r);
+        col_add(acc[0], *p, r);
       }
     }
-    // write this chunk's partials
+  }
 #pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-      int64_t c = c0 + k;
-      size_t off = (size_t)blockIdx.y * cols + c;
-      if constexpr (ARG) {
-        ((float*)partials)[2 * (2 * off)] = m[k];
-        ((int64_t*)partials)[2 * off + 1] = ix[k];
-      } else if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
-        ((double*)partials)[off] = s[k];
-      } else {
-        ((float*)partials)[2 * off] = m[k];
-      }
-    }
+  for (int k = 0; k < VEC; ++k) sh[warp][lane * VEC + k] = acc[k];
+  __syncthreads();
+  // fold the 8 warps (warp order) and write this chunk's partial
+  for (int j = threadIdx.x; j < 32 * VEC; j += blockDim.x) {
+    const int64_t c = (int64_t)blockIdx.x * 32 * VEC + j;
+    if (c >= cols) continue;
+    ColAcc<OP> t = sh[0][j];
+    for (int w = 1; w < 8; ++w) col_merge(t, sh[w][j]);
+    col_store(partials, (size_t)blockIdx.y * cols + c, t);
   }
   __threadfence();
-  __shared__ unsigned is_last;
   __syncthreads();
   if (threadIdx.x == 0) is_last = (atomicAdd(&counters[blockIdx.x], 1u) == gridDim.y - 1);
   __syncthreads();
   if (!is_last) return;
   __threadfence();
-  if (active) {
-#pragma unroll
-    for (int k = 0; k < VEC; ++k) {
-      int64_t c = c0 + k;
-      double ts = 0.0;
-      float tm = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
-      int64_t ti = INT64_MAX;
-      for (unsigned y = 0; y < gridDim.y; ++y) {
-        size_t off = (size_t)y * cols + c;
-        if constexpr (ARG) {
-          float pv = __ldcg(&((float*)partials)[2 * (2 * off)]);
-          int64_t pi = __ldcg(&((int64_t*)partials)[2 * off + 1]);
-          if (arg_better<L>(pv, pi, tm, ti)) { tm = pv; ti = pi; }
-        } else if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
-          ts += __ldcg(&((double*)partials)[off]);
-        } else {
-          float pv = __ldcg(&((float*)partials)[2 * off]);
-          tm = (OP == TL_RED_MAX) ? fmaxf(tm, pv) : fminf(tm, pv);
-        }
-      }
-      if constexpr (OP == TL_RED_SUM) out[c] = (float)ts;
-      else if constexpr (OP == TL_RED_MEAN) out[c] = (float)(ts / (double)rows);
-      else if constexpr (ARG) out[c] = (float)ti;
-      else out[c] = tm;
+  for (int j = threadIdx.x; j < 32 * VEC; j += blockDim.x) {
+    const int64_t c = (int64_t)blockIdx.x * 32 * VEC + j;
+    if (c >= cols) continue;
+    ColAcc<OP> t;
+    col_init(t);
+    unsigned y = 0;
+    for (; y + 3 < gridDim.y; y += 4) {  // 4 partial loads in flight
+      ColAcc<OP> a = col_load<OP>(partials, (size_t)y * cols + c);
+      ColAcc<OP> b = col_load<OP>(partials, (size_t)(y + 1) * cols + c);
+      ColAcc<OP> d = col_load<OP>(partials, (size_t)(y + 2) * cols + c);
+      ColAcc<OP> e = col_load<OP>(partials, (size_t)(y + 3) * cols + c);
+      col_merge(t, a); col_merge(t, b); col_merge(t, d); col_merge(t, e);
     }
+    for (; y < gridDim.y; ++y) col_merge(t, col_load<OP>(partials, (size_t)y * cols + c));
+    if constexpr (OP == TL_RED_SUM) out[c] = (float)t.s;
+    else if constexpr (OP == TL_RED_MEAN) out[c] = (float)(t.s / (double)rows);
+    else if constexpr (OP == TL_RED_ARGMAX || OP == TL_RED_ARGMIN) out[c] = (float)t.i;
+    else out[c] = t.m;
   }
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
 }
 
 // ------------------------------------------------------------ axis = None -
 template <int OP, bool VEC>
-__global__ void __launch_bounds__(256) reduce_full_kernel(const float* __restrict__ in,
+__global__ void __launch_bounds__(256, kFullBlocksPerSm) reduce_full_kernel(const float* __restrict__ in,
                                                           float* __restrict__ out, int64_t n,
                                                           unsigned* counter, void* partials) {
   constexpr bool ARG = (OP == TL_RED_ARGMAX || OP == TL_RED_ARGMIN);
@@ -267,7 +313,37 @@ __global__ void __launch_bounds__(256) reduce_full_kernel(const float* __restric
   int64_t ix = INT64_MAX;
   if constexpr (VEC) {
     const int64_t n4 = n >> 2;
-    for (int64_t i = tid; i < n4; i += stride) {
+    int64_t i = tid;
+    if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+      // 4 loads in flight, 4 independent accumulation chains
+      double s1 = 0.0, s2 = 0.0, s3 = 0.0;
+#pragma unroll 1
+      for (; i + 3 * stride < n4; i += 4 * stride) {
+        float4 a = ld_stream4(in + 4 * i), b = ld_stream4(in + 4 * (i + stride));
+        float4 c = ld_stream4(in + 4 * (i + 2 * stride)), d = ld_stream4(in + 4 * (i + 3 * stride));
+        s += (double)a.x; s += (double)a.y; s += (double)a.z; s += (double)a.w;
+        s1 += (double)b.x; s1 += (double)b.y; s1 += (double)b.z; s1 += (double)b.w;
+        s2 += (double)c.x; s2 += (double)c.y; s2 += (double)c.z; s2 += (double)c.w;
+        s3 += (double)d.x; s3 += (double)d.y; s3 += (double)d.z; s3 += (double)d.w;
+      }
+      s = (s + s1) + (s2 + s3);
+    } else if constexpr (OP == TL_RED_MAX || OP == TL_RED_MIN) {
+#pragma unroll 1
+      for (; i + 3 * stride < n4; i += 4 * stride) {
+        float4 a = ld_stream4(in + 4 * i), b = ld_stream4(in + 4 * (i + stride));
+        float4 c = ld_stream4(in + 4 * (i + 2 * stride)), d = ld_stream4(in + 4 * (i + 3 * stride));
+        if constexpr (OP == TL_RED_MAX) {
+          const float ab = fmaxf(fmaxf(fmaxf(a.x, a.y), fmaxf(a.z, a.w)), fmaxf(fmaxf(b.x, b.y), fmaxf(b.z, b.w)));
+          const float cd = fmaxf(fmaxf(fmaxf(c.x, c.y), fmaxf(c.z, c.w)), fmaxf(fmaxf(d.x, d.y), fmaxf(d.z, d.w)));
+          m = fmaxf(m, fmaxf(ab, cd));
+        } else {
+          const float ab = fminf(fminf(fminf(a.x, a.y), fminf(a.z, a.w)), fminf(fminf(b.x, b.y), fminf(b.z, b.w)));
+          const float cd = fminf(fminf(fminf(c.x, c.y), fminf(c.z, c.w)), fminf(fminf(d.x, d.y), fminf(d.z, d.w)));
+          m = fminf(m, fminf(ab, cd));
+        }
+      }
+    }
+    for (; i < n4; i += stride) {
       float4 a = ld_stream4(in + 4 * i);
       if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
         s += (double)a.x; s += (double)a.y; s += (double)a.z; s += (double)a.w;
@@ -324,30 +400,55 @@ __global__ void __launch_bounds__(256) reduce_full_kernel(const float* __restric
     is_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
   }
   __syncthreads();
-  if (!is_last || threadIdx.x != 0) return;
+  if (!is_last) return;
   __threadfence();
   if constexpr (OP == TL_RED_SUM || OP == TL_RED_MEAN) {
+    // each thread folds a fixed strided subset, then a fixed-order block fold
     double t = 0.0;
-    for (unsigned b = 0; b < gridDim.x; ++b) t += __ldcg(&((double*)partials)[b]);
-    out[0] = (OP == TL_RED_MEAN) ? (float)(t / (double)n) : (float)t;
-  } else if constexpr (ARG) {
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) t += __ldcg(&((double*)partials)[b]);
+    t = warp_sum(t);
+    if (lane == 0) sh_d[wid] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      double tt = 0.0;
+      for (int w = 0; w < nw; ++w) tt += sh_d[w];
+      out[0] = (OP == TL_RED_MEAN) ? (float)(tt / (double)n) : (float)tt;
+      *counter = 0u;
+    }
+    return;
+  }
+  if constexpr (ARG) {
     float tv = 0.f;
     int64_t ti = INT64_MAX;
-    for (unsigned b = 0; b < gridDim.x; ++b) {
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
       float pv = __ldcg(&((float*)partials)[4 * b]);
       int64_t pi = __ldcg(&((int64_t*)partials)[2 * b + 1]);
       if (arg_better<L>(pv, pi, tv, ti)) { tv = pv; ti = pi; }
     }
-    out[0] = (float)ti;
+    warp_arg<L>(tv, ti);
+    if (lane == 0) { sh_f[wid] = tv; sh_i[wid] = ti; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 0; w < nw; ++w)
+        if (arg_better<L>(sh_f[w], sh_i[w], tv, ti)) { tv = sh_f[w]; ti = sh_i[w]; }
+      out[0] = (float)ti;
+      *counter = 0u;
+    }
   } else {
     float t = (OP == TL_RED_MAX) ? -INFINITY : INFINITY;
-    for (unsigned b = 0; b < gridDim.x; ++b) {
+    for (unsigned b = threadIdx.x; b < gridDim.x; b += blockDim.x) {
       float pv = __ldcg(&((float*)partials)[2 * b]);
       t = (OP == TL_RED_MAX) ? fmaxf(t, pv) : fminf(t, pv);
     }
-    out[0] = t;
+    t = (OP == TL_RED_MAX) ? warp_max(t) : warp_min(t);
+    if (lane == 0) sh_f[wid] = t;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      for (int w = 0; w < nw; ++w) t = (OP == TL_RED_MAX) ? fmaxf(t, sh_f[w]) : fminf(t, sh_f[w]);
+      out[0] = t;
+      *counter = 0u;
+    }
   }
-  *counter = 0u;
 }
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
@@ -372,15 +473,15 @@ int launch_cols(const float* in, float* out, int64_t rows, int64_t cols, void* s
   void* partials = (char*)scratch + kCounterBytes;
   dim3 grid(p.gx, p.gy);
   if (vec)
-    reduce_cols_kernel<OP, 4><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+    reduce_cols_kernel<OP, 4><<<grid, 256, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
   else
-    reduce_cols_kernel<OP, 1><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+    reduce_cols_kernel<OP, 1><<<grid, 256, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
   return after_launch();
 }
 
 unsigned full_blocks(int64_t n) {
   int64_t b = (n + 4LL * 256 - 1) / (4LL * 256);
-  int64_t cap = 8LL * sm_count();
+  int64_t cap = (int64_t)kFullBlocksPerSm * sm_count();  // exactly one resident wave
   if (cap > kFullMaxBlocks) cap = kFullMaxBlocks;
   if (b > cap) b = cap;
   if (b < 1) b = 1;
@@ -507,9 +608,9 @@ int launch_cols_noalloc(const float* in, float* out, int64_t rows, int64_t cols,
   void* partials = (char*)base + kCounterBytes;
   dim3 grid(p.gx, p.gy);
   if (vec)
-    reduce_cols_kernel<OP, 4><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+    reduce_cols_kernel<OP, 4><<<grid, 256, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
   else
-    reduce_cols_kernel<OP, 1><<<grid, p.threads, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
+    reduce_cols_kernel<OP, 1><<<grid, 256, 0, st>>>(in, out, rows, cols, p.chunk, counters, partials);
   return after_launch();
 }
 

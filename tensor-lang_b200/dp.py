@@ -136,6 +136,11 @@ class Communicator:
         self.handle = None
         if self.world == 1:
             return
+        # NVLink SHARP (NVLS) stays off unless the caller enables it: it binds
+        # memory to NVLink multicast objects, and a rank dying while bound has
+        # faulted its peers' GPUs on shared machines; the ring/tree algorithms
+        # over NVLink carry the gradient all-reduce without it.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
         L = rt.lib()
         uid = ctypes.create_string_buffer(128)
         if self.rank == 0:

@@ -37,6 +37,9 @@ import numpy as np
 from . import runtime as rt
 
 BLOCK = 256
+UNROLL = 1          # units per thread per loop trip (more raised register use and lost
+                    # occupancy on B200: 1 unit at 16 blocks/SM measured fastest)
+BLOCKS_PER_SM = 16  # grid size cap, as a multiple of the SM count
 
 # opcode -> (arity, C expression template over a, b, c)
 OPS = {
@@ -213,13 +216,13 @@ class Region:
                 if k not in keys:
                     keys.append(k)
         self.params = keys
-        # blocks per segment: enough 2x-unrolled float4 work per thread, at
-        # most 8 resident blocks per SM overall
+        # blocks per segment: enough unrolled float4 work per thread, at most
+        # BLOCKS_PER_SM blocks per SM overall
         work = []
         for s in self.segs:
             units = (s.total + 3) // 4 if self._vec_ok(s) else s.total
-            work.append(max(1, (units + 2 * BLOCK - 1) // (2 * BLOCK)))
-        cap = 8 * sm_count
+            work.append(max(1, (units + UNROLL * BLOCK - 1) // (UNROLL * BLOCK)))
+        cap = BLOCKS_PER_SM * sm_count
         total = sum(work)
         if total > cap:
             scale = cap / total
@@ -259,99 +262,102 @@ class Region:
             if inp.access == "scalar":
                 lines.append(f"    const float s{ii} = p{pidx[inp.key]}[0];")
 
-        def coord_code(e: str) -> List[str]:
-            """offsets for row / strided accesses of flat element e"""
+        def coord_code(e: str, x: str) -> List[str]:
+            """row / column / strided offsets of flat element ``e`` (suffix x)"""
             out = []
-            need_row = any(i.access == "row" for i in s.inputs)
-            need_col = any(i.access == "col" for i in s.inputs)
-            if need_row:
-                out.append(f"      const long long r_ = {e} / {C}LL;")
-            if need_col:
-                out.append(f"      const long long c_ = {e} % {C}LL;")
+            if any(i.access == "row" for i in s.inputs):
+                out.append(f"      const long long r{x} = {e} / {C}LL;")
+            if any(i.access == "col" for i in s.inputs):
+                out.append(f"      const long long c{x} = {e} % {C}LL;")
             strided = [ii for ii, i in enumerate(s.inputs) if i.access == "strided"]
             if strided:
-                out.append(f"      long long rem_ = {e};")
+                out.append(f"      long long rem{x} = {e};")
                 for ax in reversed(range(len(shape))):
-                    out.append(f"      const long long k{ax}_ = rem_ % {int(shape[ax])}LL; "
-                               f"rem_ /= {int(shape[ax])}LL;")
+                    out.append(f"      const long long k{ax}{x} = rem{x} % {int(shape[ax])}LL; "
+                               f"rem{x} /= {int(shape[ax])}LL;")
                 for ii in strided:
-                    terms = [f"k{ax}_ * {st}LL" for ax, st in enumerate(s.inputs[ii].strides) if st]
-                    out.append(f"      const long long o{ii}_ = {' + '.join(terms) if terms else '0LL'};")
+                    terms = [f"k{ax}{x} * {st}LL" for ax, st in enumerate(s.inputs[ii].strides) if st]
+                    out.append(f"      const long long o{ii}{x} = {' + '.join(terms) if terms else '0LL'};")
             return out
 
-        def load_code(e: str) -> List[str]:
+        def is4(inp: Input) -> bool:
+            return vec and (inp.access in ("full", "col") or
+                            (inp.access == "strided" and inp.strides[-1] == 1))
+
+        def load_code(e: str, x: str) -> List[str]:
             out = []
             for ii, inp in enumerate(s.inputs):
                 p = f"p{pidx[inp.key]}"
                 if inp.access == "full":
-                    out.append(f"      const float4 v{ii} = tl_ld4({p} + {e});" if vec
-                               else f"      const float v{ii} = __ldg({p} + {e});")
+                    out.append(f"      const float4 v{ii}{x} = tl_ld4({p} + {e});" if vec
+                               else f"      const float v{ii}{x} = __ldg({p} + {e});")
                 elif inp.access == "row":
-                    out.append(f"      const float v{ii} = __ldg({p} + r_);")
+                    out.append(f"      const float v{ii}{x} = __ldg({p} + r{x});")
                 elif inp.access == "col":
-                    out.append(f"      const float4 v{ii} = tl_ldc4({p} + c_);" if vec
-                               else f"      const float v{ii} = __ldg({p} + c_);")
+                    out.append(f"      const float4 v{ii}{x} = tl_ldc4({p} + c{x});" if vec
+                               else f"      const float v{ii}{x} = __ldg({p} + c{x});")
                 elif inp.access == "strided":
-                    if vec and inp.strides[-1] == 1:
-                        out.append(f"      const float4 v{ii} = tl_ldc4({p} + o{ii}_);")
+                    if is4(inp):
+                        out.append(f"      const float4 v{ii}{x} = tl_ldc4({p} + o{ii}{x});")
                     else:
-                        out.append(f"      const float v{ii} = __ldg({p} + o{ii}_);")
+                        out.append(f"      const float v{ii}{x} = __ldg({p} + o{ii}{x});")
             return out
 
-        def val(ref: Ref, lane: int) -> str:
+        def val(ref: Ref, lane: int, x: str) -> str:
             if ref.kind == "const":
                 return _fmt_const(ref.value)
             if ref.kind == "tmp":
-                return f"t{ref.idx}_{lane}"
+                return f"t{ref.idx}_{lane}{x}"
             inp = s.inputs[ref.idx]
             if inp.access == "scalar":
                 return f"s{ref.idx}"
-            is4 = vec and (inp.access in ("full", "col") or
-                           (inp.access == "strided" and inp.strides[-1] == 1))
-            return f"v{ref.idx}.{comp[lane]}" if is4 else f"v{ref.idx}"
+            return f"v{ref.idx}{x}.{comp[lane]}" if is4(inp) else f"v{ref.idx}{x}"
 
-        def body_code() -> List[str]:
+        def body_code(x: str) -> List[str]:
             out = []
             for lane in range(lanes):
                 for ti, (opc, args) in enumerate(s.body):
                     tmpl = OPS[opc][1]
-                    kw = {"a": val(args[0], lane)}
+                    kw = {"a": val(args[0], lane, x)}
                     if len(args) > 1:
-                        kw["b"] = val(args[1], lane)
-                    out.append(f"      const float t{ti}_{lane} = {tmpl.format(**kw)};")
+                        kw["b"] = val(args[1], lane, x)
+                    out.append(f"      const float t{ti}_{lane}{x} = {tmpl.format(**kw)};")
             return out
 
-        def store_code(e: str) -> List[str]:
+        def store_code(e: str, x: str) -> List[str]:
             out = []
             for key, ref in s.outputs:
                 p = f"p{pidx[key]}"
                 if vec:
-                    vals = ", ".join(val(ref, l) for l in range(4))
+                    vals = ", ".join(val(ref, l, x) for l in range(4))
                     out.append(f"      tl_st4({p} + {e}, make_float4({vals}));")
                 else:
-                    out.append(f"      {p}[{e}] = {val(ref, 0)};")
+                    out.append(f"      {p}[{e}] = {val(ref, 0, x)};")
             return out
 
         units = s.total // 4 if vec else s.total
         step = 4 if vec else 1
-        # 2x unrolled grid-stride loop: issue both iterations' loads first
-        lines.append(f"    long long u = t0;")
-        lines.append(f"    for (; u + nb < {units}LL; u += 2 * nb) {{")
-        for tag, uexpr in (("a", "u"), ("b", "(u + nb)")):
-            lines.append(f"     {{ const long long e = {uexpr} * {step}LL;")
-            lines += coord_code("e")
-            lines += load_code("e")
-            lines += body_code()
-            lines += store_code("e")
-            lines.append("     }")
+        # UNROLL-way unrolled grid-stride loop: each trip issues the loads of
+        # all UNROLL units before any arithmetic; the remainder runs one unit
+        # at a time
+        lines.append("    long long u = t0;")
+        lines.append(f"    for (; u + {UNROLL - 1}LL * nb < {units}LL; u += {UNROLL}LL * nb) {{")
+        for q in range(UNROLL):
+            lines.append(f"      const long long e_{q} = (u + {q}LL * nb) * {step}LL;")
+        for q in range(UNROLL):
+            lines += coord_code(f"e_{q}", f"_{q}")
+        for q in range(UNROLL):
+            lines += load_code(f"e_{q}", f"_{q}")
+        for q in range(UNROLL):
+            lines += body_code(f"_{q}")
+            lines += store_code(f"e_{q}", f"_{q}")
         lines.append("    }")
         lines.append(f"    for (; u < {units}LL; u += nb) {{")
-        lines.append(f"     {{ const long long e = u * {step}LL;")
-        lines += coord_code("e")
-        lines += load_code("e")
-        lines += body_code()
-        lines += store_code("e")
-        lines.append("     }")
+        lines.append(f"      const long long e_r = u * {step}LL;")
+        lines += coord_code("e_r", "_r")
+        lines += load_code("e_r", "_r")
+        lines += body_code("_r")
+        lines += store_code("e_r", "_r")
         lines.append("    }")
         lines.append("    return;")
         lines.append("  }")
@@ -359,7 +365,8 @@ class Region:
 
     def codegen(self, sm_count: int) -> Tuple[str, str]:
         self._plan(sm_count)
-        sig = "||".join(s.signature() for s in self.segs) + f"|G{self.grid}|P{len(self.params)}"
+        sig = "||".join(s.signature() for s in self.segs) + \
+            f"|G{self.grid}|P{len(self.params)}|U{UNROLL}|B{BLOCK}"
         digest = hashlib.sha1(sig.encode()).hexdigest()[:20]
         name = f"tl_region_{digest}"
         written = set()
