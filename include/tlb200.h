@@ -226,6 +226,17 @@ int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
  * operand as the TF32 "hi" part); 1 force the CUDA-core path; 2 automatic,
  * with hi and lo both rounded to TF32 explicitly in the pre-pass. */
 int  tl_gemm_force_simt(int force);
+/* Tensor-core operand scheme for fp32 products (no reference counterpart:
+ * the reference calls cuBLAS SGEMM / its own fp32 kernels).
+ *   TL_GEMM_3XTF32     hi*hi + hi*lo + lo*hi, three TF32 MMAs per k-step
+ *   TL_GEMM_TF32_BF16  hi*hi on TF32, both correction terms in one bf16 MMA
+ *                      over [bf16(A)|bf16(loA)] . [bf16(loB)|bf16(B)] (default)
+ * Both stay within rel 1e-5 of an fp64 product on N(0,1) data.  Returns
+ * TL_ERR_INVALID_ARG for an unknown scheme; *previous (if non-null) receives
+ * the scheme that was in force.  Applies to launches made after the call. */
+#define TL_GEMM_3XTF32 0
+#define TL_GEMM_TF32_BF16 1
+int  tl_gemm_set_scheme(int scheme, int* previous);
 /* Device-side error flag (TL_ERR_TIMEOUT after a bounded wait in a kernel
  * gave up; 0 if none).  reset != 0 clears it. */
 int  tl_device_error(int* code, int reset);

@@ -12,6 +12,16 @@
 // lo*hi, accumulating in fp32 in TMEM (the dropped lo*lo term is ~2^-22
 // relative).
 //
+// The TF32+bf16 scheme (the default) keeps hi*hi on the TF32 path and folds
+// both correction terms into one bf16 MMA over a K-concatenated pair:
+//   [bf16(A) | bf16(loA)] . [bf16(loB) | bf16(B)]  =  A*loB + loA*B  (+ ~2^-19)
+// A pre-pass writes each operand's pair tile K-major (transposing MN-major
+// operands), 32 values then 32 lows per 32-deep k-block, so one 128-byte
+// swizzled bf16 row holds a k-block's pair.  Per 8-deep k-step this is one
+// TF32 MMA plus half a bf16 MMA of the same shape: 2 TF32 MMA-times instead of
+// 3.  Per product the error is below 9 * 2^-20 relative (lo*lo dropped,
+// bf16 rounding of the correction operands).
+//
 // One CTA computes a 128 x 256 tile with 10 warps:
 //   warp 0 lane 0   TMA producer (2-stage ring of hi/lo tiles of A and B)
 //   warp 1          TMEM allocation; lane 0 issues the MMAs
@@ -26,6 +36,7 @@
 // records TL_ERR_TIMEOUT in a device flag (tl_device_error) and falls
 // through to free its TMEM and exit.
 #include <cuda.h>
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -113,6 +124,15 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+__device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
                : "memory");
@@ -175,6 +195,19 @@ __host__ __device__ constexpr uint32_t idesc_tf32() {
          | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
+// Instruction descriptor: kind::f16 with bf16 A and B (both K-major), fp32
+// accumulate, M=128, N=BN.
+__host__ __device__ constexpr uint32_t idesc_bf16() {
+  return (1u << 4)     // D format: f32
+         | (1u << 7)   // A format: bf16
+         | (1u << 10)  // B format: bf16
+         | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// Operand schemes
+constexpr int kScheme3xTF32 = 0;    // lo tiles fp32: hi*hi + hi*lo + lo*hi, all TF32
+constexpr int kSchemeTF32BF16 = 1;  // pair tiles bf16: hi*hi TF32 + one bf16 pair MMA
+
 struct Params {
   int M, N, K;
   float* C;
@@ -193,11 +226,15 @@ struct Params {
 // KC k-blocks, alternately into two TMEM accumulators, and the epilogue warps
 // add each finished chunk into fp32 registers with round-to-nearest while
 // the tensor core fills the other accumulator.
-template <int TA, int TB>
+//
+// SCHEME kSchemeTF32BF16: tmAlo / tmBlo are the bf16 pair matrices, always
+// K-major ([rows][2*Kp], one 64-wide box per k-block).
+template <int TA, int TB, int SCHEME>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBlo,
                    Params p) {
+  constexpr bool PAIR = SCHEME == kSchemeTF32BF16;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -251,23 +288,27 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int k0 = kb * BK;
         if (TA == 0) {
           tma_load_2d(sA, &tmA, fb, k0, m0);
-          tma_load_2d(sAl, &tmAlo, fb, k0, m0);
+          if (!PAIR) tma_load_2d(sAl, &tmAlo, fb, k0, m0);
         } else {
 #pragma unroll
           for (int c = 0; c < BM / 32; ++c) {
             tma_load_2d(sA + c * 4096, &tmA, fb, m0 + 32 * c, k0);
-            tma_load_2d(sAl + c * 4096, &tmAlo, fb, m0 + 32 * c, k0);
+            if (!PAIR) tma_load_2d(sAl + c * 4096, &tmAlo, fb, m0 + 32 * c, k0);
           }
         }
         if (TB == 1) {
           tma_load_2d(sB, &tmB, fb, k0, n0);
-          tma_load_2d(sBl, &tmBlo, fb, k0, n0);
+          if (!PAIR) tma_load_2d(sBl, &tmBlo, fb, k0, n0);
         } else {
 #pragma unroll
           for (int c = 0; c < BN / 32; ++c) {
             tma_load_2d(sB + c * 4096, &tmB, fb, n0 + 32 * c, k0);
-            tma_load_2d(sBl + c * 4096, &tmBlo, fb, n0 + 32 * c, k0);
+            if (!PAIR) tma_load_2d(sBl + c * 4096, &tmBlo, fb, n0 + 32 * c, k0);
           }
+        }
+        if (PAIR) {  // k-block kb of the pair matrices starts at column 64*kb = 2*k0
+          tma_load_2d(sAl, &tmAlo, fb, 2 * k0, m0);
+          tma_load_2d(sBl, &tmBlo, fb, 2 * k0, n0);
         }
       }
     }
@@ -294,16 +335,30 @@ __global__ void __launch_bounds__(THREADS, 1)
           unsigned char* st = smem + s * STAGE_BYTES;
           const uint32_t sA = smem_u32(st), sAl = sA + A_TILE;
           const uint32_t sB = sAl + A_TILE, sBl = sB + B_TILE;
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int k = 0; k < BK / 8; ++k) {
-            const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
-            const uint64_t al = TA ? mnmajor_desc(sAl, k) : kmajor_desc(sAl, k);
-            const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
-            const uint64_t bl = TB ? kmajor_desc(sBl, k) : mnmajor_desc(sBl, k);
-            const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
-            mma_tf32(acc, a, bh, idesc, first);
-            mma_tf32(acc, a, bl, idesc, 1u);
-            mma_tf32(acc, al, bh, idesc, 1u);
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma_tf32(acc, a, bh, idesc, first);
+            }
+            // 64 bf16 per row (32 values, 32 lows): 4 k-steps of 16, each a 32-byte advance
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma_bf16(acc, kmajor_desc(sAl, k), kmajor_desc(sBl, k), idesc_bf16());
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+              const uint64_t al = TA ? mnmajor_desc(sAl, k) : kmajor_desc(sAl, k);
+              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+              const uint64_t bl = TB ? kmajor_desc(sBl, k) : mnmajor_desc(sBl, k);
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma_tf32(acc, a, bh, idesc, first);
+              mma_tf32(acc, a, bl, idesc, 1u);
+              mma_tf32(acc, al, bh, idesc, 1u);
+            }
           }
           mma_commit(smem_u32(&empty[s]));  // frees the stage when these MMAs finish
         }
@@ -420,6 +475,87 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__
     dst[i] = src[i] - __uint_as_float(__float_as_uint(src[i]) & 0xFFFFE000u);
 }
 
+__device__ __forceinline__ float lo_of(float x) {
+  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+}
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
+         ((uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(b)) << 16);
+}
+
+// Pair matrix of a K-major operand X[r][k] (row stride ld): row r of P holds,
+// per 32-deep k-block j, 32 bf16 of one kind then 32 of the other at columns
+// 64j..64j+63 -- bf16(x) first for an A operand, bf16(lo) first for B
+// (lo_first).  Columns for k >= K are zero.  Rows r are grid-strided, the 4-k
+// groups of a row are spread over the threads.
+__global__ void __launch_bounds__(256) pair_rows_kernel(const float* __restrict__ X, int64_t ld,
+                                                        int64_t R, int64_t K, int64_t kp,
+                                                        int lo_first, __nv_bfloat16* __restrict__ P) {
+  const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
+  const int64_t nq = kp >> 2;
+  for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
+    const float* src = X + r * ld;
+    __nv_bfloat16* dst = P + r * 2 * kp;
+    for (int64_t q = threadIdx.x; q < nq; q += blockDim.x) {
+      const int64_t k = 4 * q;
+      float x[4];
+      if (vec && k + 3 < K) {
+        const float4 v = ld_stream4(src + k);
+        x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) x[i] = (k + i < K) ? src[k + i] : 0.f;
+      }
+      const uint2 hv = make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]));
+      const uint2 lv = make_uint2(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])));
+      __nv_bfloat16* o = dst + 64 * (k >> 5) + (k & 31);
+      *reinterpret_cast<uint2*>(o) = lo_first ? lv : hv;
+      *reinterpret_cast<uint2*>(o + 32) = lo_first ? hv : lv;
+    }
+  }
+}
+
+// Pair matrix of an MN-major operand (X stored [K][R], X_eff[r][k] = X[k*ld + r]):
+// a 32 (k) x 128 (r) tile is staged in shared memory (odd row pitch:
+// conflict-free both ways) and written as 128 rows of one 128-byte k-block.
+__global__ void __launch_bounds__(256) pair_cols_kernel(const float* __restrict__ X, int64_t ld,
+                                                        int64_t R, int64_t K, int64_t kp,
+                                                        int lo_first, __nv_bfloat16* __restrict__ P) {
+  __shared__ float S[32][129];
+  const int64_t nrt = (R + 127) / 128, nkb = kp / 32;
+  for (int64_t t = blockIdx.x; t < nrt * nkb; t += gridDim.x) {
+    const int64_t rt = t % nrt, j = t / nrt;
+    const int64_t r0 = rt * 128, k0 = j * 32;
+    __syncthreads();
+#pragma unroll 4
+    for (int e = threadIdx.x; e < 32 * 128; e += 256) {
+      const int kk = e >> 7, rr = e & 127;
+      const int64_t k = k0 + kk, r = r0 + rr;
+      S[kk][rr] = (k < K && r < R) ? X[k * ld + r] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int c = threadIdx.x; c < 128 * 8; c += 256) {
+      const int rr = c >> 3, part = c & 7;  // 8 chunks of 16 bytes per output row
+      const int64_t r = r0 + rr;
+      if (r >= R) continue;
+      const int h = part >> 2, kk0 = (part & 3) * 8;
+      const bool low = (h == 0) == (lo_first != 0);
+      uint32_t w[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float x0 = S[kk0 + 2 * i][rr], x1 = S[kk0 + 2 * i + 1][rr];
+        if (low) {
+          x0 = lo_of(x0);
+          x1 = lo_of(x1);
+        }
+        w[i] = pack_bf16(x0, x1);
+      }
+      *reinterpret_cast<uint4*>(P + r * 2 * kp + 64 * j + 32 * h + kk0) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
 // ------------------------------------------------------------- host side ---
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -460,6 +596,19 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int
                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D bf16 tensor map over a pair matrix [rows][2*kp]: 64-wide boxes (128 B),
+// 128-byte swizzle, K-major.
+bool make_pair_map(CUtensorMap* m, const __nv_bfloat16* base, int64_t rows, int64_t kp,
+                   uint32_t box_outer) {
+  cuuint64_t dims[2] = {(cuuint64_t)(2 * kp), (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(2 * kp) * 2};
+  cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // Split workspace, grown on demand outside stream capture and never freed
 // (graphs captured earlier may still reference an older buffer).
 int workspace(size_t floats, float** out, cudaStream_t st) {
@@ -484,6 +633,7 @@ int workspace(size_t floats, float** out, cudaStream_t st) {
 }
 
 int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both rounded
+int g_scheme = kSchemeTF32BF16;
 
 unsigned split_grid(size_t n) {
   unsigned g = (unsigned)((n / 4 + 255) / 256);
@@ -491,10 +641,54 @@ unsigned split_grid(size_t n) {
   return g < 1 ? 1 : (g < cap ? g : cap);
 }
 
+unsigned pair_grid(int64_t units) {
+  const int64_t cap = 8LL * sm_count();
+  return (unsigned)(units < 1 ? 1 : (units < cap ? units : cap));
+}
+
+template <int TA, int TB>
+int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B,
+                int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
+                cudaStream_t st) {
+  const int64_t kp = (K + 31) / 32 * 32;
+  const size_t a_bytes = ((size_t)M * kp * 4 + 1023) / 1024 * 1024;  // [M][2kp] bf16
+  const size_t b_bytes = ((size_t)N * kp * 4 + 1023) / 1024 * 1024;
+  float* ws = nullptr;
+  TL_TRY(workspace((a_bytes + b_bytes) / 4, &ws, st));
+  __nv_bfloat16* ap = reinterpret_cast<__nv_bfloat16*>(ws);
+  __nv_bfloat16* bp = reinterpret_cast<__nv_bfloat16*>((char*)ws + a_bytes);
+  if (TA == 0)
+    pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, ap);
+  else
+    pair_cols_kernel<<<pair_grid((M + 127) / 128 * (kp / 32)), 256, 0, st>>>(A, lda, M, K, kp, 0, ap);
+  TL_TRY(after_launch());
+  if (TB == 1)
+    pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, bp);
+  else
+    pair_cols_kernel<<<pair_grid((N + 127) / 128 * (kp / 32)), 256, 0, st>>>(B, ldb, N, K, kp, 1, bp);
+  TL_TRY(after_launch());
+
+  const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
+  const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
+  CUtensorMap ma, map_, mb, mbp;
+  if (!make_map(&ma, A, a_rows, a_cols, lda, 32, TA ? 32 : BM, TA == 1) ||
+      !make_map(&mb, B, b_rows, b_cols, ldb, 32, TB ? BN : 32, TB == 0) ||
+      !make_pair_map(&map_, ap, M, kp, BM) || !make_pair_map(&mbp, bp, N, kp, BN))
+    return TL_ERR_UNSUPPORTED;
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
+  auto kern = gemm_tc_kernel<TA, TB, kSchemeTF32BF16>;
+  TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, map_, mb, mbp, p);
+  return after_launch();
+}
+
 template <int TA, int TB>
 int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
            float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, cudaStream_t st) {
   if (!load_encode()) return TL_ERR_UNSUPPORTED;
+  if (g_scheme == kSchemeTF32BF16 && g_split_mode == 0)
+    return launch_pair<TA, TB>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
   const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
   // the elements a row-major [rows][cols] matrix with leading dim ld spans
@@ -536,7 +730,7 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
       !make_map(&mbl, b_lo, b_rows, b_cols, ldb, b_inner, b_outer, b_mn))
     return TL_ERR_UNSUPPORTED;
   Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
-  auto kern = gemm_tc_kernel<TA, TB>;
+  auto kern = gemm_tc_kernel<TA, TB, kScheme3xTF32>;
   TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
   dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
   kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mal, mb, mbl, p);
@@ -573,6 +767,13 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
 }
 
 void gemm_set_split_mode(int mode) { g_split_mode = mode; }
+
+int gemm_set_scheme(int scheme) {
+  if (scheme != kScheme3xTF32 && scheme != kSchemeTF32BF16) return -1;
+  const int prev = g_scheme;
+  g_scheme = scheme;
+  return prev;
+}
 
 }  // namespace tl
 

@@ -148,7 +148,7 @@ ColPlan col_plan(int64_t rows, int64_t cols, bool vec_ok) {
   p.vec = vec_ok ? 4 : 1;
   p.gx = ceil_div_u(cols, 32LL * p.vec);
   // one resident wave: kColBlocksPerSm blocks of 256 threads on every SM
-  int64_t want = (kColBlocksPerSm * kAssumedSms + p.gx - 1) / p.gx;
+  int64_t want = (int64_t)kColBlocksPerSm * kAssumedSms / p.gx;  // rounded down: no second wave
   int64_t maxy = (rows + 63) / 64;  // at least 64 rows per chunk
   if (want > maxy) want = maxy;
   if (want > 256) want = 256;

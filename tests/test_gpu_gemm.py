@@ -2,8 +2,10 @@
 
 Covers every storage combination the executor uses (A as stored or
 transposed, B as stored or transposed), ragged M/N/K (the tensor-core tiles
-are 128x256x32, so partial tiles exercise TMA zero fill and masked stores),
-bias, relu and accumulate.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
+are 128x256x32, so partial tiles exercise TMA zero fill and masked stores;
+K not a multiple of 32 exercises the zero columns of the bf16 pair
+matrices), bias, relu and accumulate, under the default TF32+bf16 operand
+scheme and the three-TF32 scheme.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
 the split-TF32 product is expected near 1e-6.  Also checks which path a
 shape takes and that no kernel left a device error.
 """
@@ -85,13 +87,41 @@ def test_gemm_cuda_core_shapes(M, N, K):
 
 @pytest.mark.parametrize("ta,tb,M,N,K", [(0, 0, 8192, 10, 4096), (1, 0, 2048, 10, 16384),
                                          (1, 0, 333, 7, 5000), (0, 1, 8192, 1024, 10),
-                                         (0, 1, 70000, 40, 3), (0, 0, 16, 10, 4096)])
+                                         (0, 1, 70000, 40, 3), (0, 0, 16, 10, 4096),
+                                         (0, 0, 1000, 10, 4092), (0, 0, 777, 24, 1000),
+                                         (0, 0, 300, 10, 4095), (1, 0, 1024, 10, 40000),
+                                         (1, 0, 516, 16, 3000), (1, 0, 4096, 24, 2000),
+                                         (0, 1, 1000, 4096, 10), (0, 1, 65, 1028, 12),
+                                         (0, 1, 100, 1030, 10)])
 @pytest.mark.parametrize("bias,acc", [(True, False), (False, True)])
 def test_gemm_skinny(ta, tb, M, N, K, bias, acc):
     """Classifier-head products (N or K of 10) on the bandwidth-bound kernels."""
     out, ref, path, err = _run(ta, tb, M, N, K, bias=bias, acc=acc)
     assert path == 1
     assert_close(out, ref, 1e-5, f"skinny {ta}{tb} {M}x{N}x{K}")
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(200, 300, 100), (332, 1000, 780), (256, 128, 16384)])
+def test_gemm_three_tf32_scheme(ta, tb, M, N, K):
+    """The three-TF32-MMA scheme (hi*hi + hi*lo + lo*hi) stays selectable."""
+    tl = load_backend()
+    L = tl.runtime.lib()
+    prev = ctypes.c_int(-1)
+    tl.runtime.check(L.tl_gemm_set_scheme(0, ctypes.byref(prev)))
+    try:
+        out, ref, path, err = _run(ta, tb, M, N, K, bias=True)
+        assert err == 0 and path == 0
+        assert_close(out, ref, 1e-5, f"3xTF32 {ta}{tb} {M}x{N}x{K}")
+    finally:
+        tl.runtime.check(L.tl_gemm_set_scheme(prev.value, None))
+    assert prev.value == 1, "TF32+bf16 is the default scheme"
+
+
+def test_gemm_scheme_rejects_unknown():
+    tl = load_backend()
+    L = tl.runtime.lib()
+    assert L.tl_gemm_set_scheme(7, None) != 0
 
 
 def test_gemm_explicit_split_mode():
