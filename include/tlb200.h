@@ -237,6 +237,12 @@ int  tl_gemm_force_simt(int force);
 #define TL_GEMM_3XTF32 0
 #define TL_GEMM_TF32_BF16 1
 int  tl_gemm_set_scheme(int scheme, int* previous);
+/* Tile shape of the tensor-core path (no reference counterpart).  enable = 1
+ * (default): products with more than 128 rows use 256 x 256 tiles computed by
+ * a cluster of two CTAs with tcgen05.mma.cta_group::2, each CTA loading half
+ * of B; enable = 0: 128 x 256 single-CTA tiles only.  *previous (if non-null)
+ * receives the setting that was in force. */
+int  tl_gemm_set_cta_pair(int enable, int* previous);
 /* Device-side error flag (TL_ERR_TIMEOUT after a bounded wait in a kernel
  * gave up; 0 if none).  reset != 0 clears it. */
 int  tl_device_error(int* code, int reset);

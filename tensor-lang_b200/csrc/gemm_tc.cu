@@ -51,7 +51,11 @@ __device__ int g_device_error = 0;
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
-constexpr int KC = 2;                          // k-blocks per TMEM accumulation chunk
+// k-blocks per TMEM accumulation chunk (128 deep): each drain reads the whole
+// accumulator out of tensor memory and slows the MMAs while it runs, so
+// chunks are as long as the accuracy allows (max rel err ~2e-6 at K=65536
+// with 4; one chunk for all of K reaches 2e-4)
+constexpr int KC = 4;
 constexpr int A_TILE = BM * BK * 4;            // 16 KB
 constexpr int B_TILE = BN * BK * 4;            // 32 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // hi + lo of A and B: 96 KB
@@ -437,6 +441,306 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
 }
 
+// ------------------------------------------------------- CTA-pair kernel ---
+// A cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2
+// on the two SMs of a pair.  CTA r (rank in the cluster) loads rows
+// m0+128r..+127 of A and rows n0+128r..+127 of B (the N axis) for every
+// k-block into its own shared memory; the leader (rank 0) issues the MMAs,
+// which read both CTAs' tiles and accumulate 128 x 256 in each CTA's tensor
+// memory.  Per CTA a k-block moves 64 KB instead of the single-CTA tile's
+// 96 KB for the same MMA work, and three stages fit.
+//
+// Barriers: every TMA load of both CTAs completes on the leader's full[s]
+// (the .cta_group::2 form of the load may signal the peer CTA's barrier);
+// the leader's MMA commits arrive on empty[s] and acc_full[b] of both CTAs
+// (commit multicast); both CTAs' epilogue warps arrive on the leader's
+// acc_free[b].  Cluster barriers after set-up and before TMEM release keep
+// either CTA from touching a peer that is not ready or has left.
+constexpr int STAGES2 = 3;
+constexpr int HB = 128;                            // B rows (N) held per CTA
+constexpr int B_HALF = HB * BK * 4;                // 16 KB
+constexpr int STAGE2_BYTES = 2 * A_TILE + 2 * B_HALF;  // 64 KB per CTA
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// shared::cluster address of the same shared variable in CTA `rank`
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                                 int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      : "memory");
+}
+// arrive on the barrier at this shared offset in both CTAs of the pair once
+// the leader's MMAs issued so far have completed
+__device__ __forceinline__ void mma2_commit_both(uint32_t bar) {
+  asm volatile(
+      "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}"
+      ::"r"(bar)
+      : "memory");
+}
+
+template <int A_MN, int B_MN>
+__host__ __device__ constexpr uint32_t idesc2_tf32() {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)A_MN << 15) | ((uint32_t)B_MN << 16) |
+         ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+}
+__host__ __device__ constexpr uint32_t idesc2_bf16() {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
+         ((uint32_t)(256 >> 4) << 24);
+}
+
+template <int TA, int TB, int SCHEME>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAx,
+                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBx,
+                    Params p) {
+  constexpr bool PAIR = SCHEME == kSchemeTF32BF16;
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+  uint64_t* bars = (uint64_t*)(smem + STAGES2 * STAGE2_BYTES);
+  uint64_t* full = bars;                    // [STAGES2] loads of both CTAs -> leader's MMA
+  uint64_t* empty = bars + STAGES2;         // [STAGES2] MMA -> each CTA's producer
+  uint64_t* acc_full = bars + 2 * STAGES2;  // [2] MMA -> each CTA's epilogue
+  uint64_t* acc_free = acc_full + 2;        // [2] both CTAs' epilogues -> leader's MMA
+  uint32_t* tmem_slot = (uint32_t*)(acc_free + 2);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // clusters walk the N tiles first, so a wave's clusters share A row blocks in L2
+  const int n_tiles = (p.N + 255) / 256;
+  const int cid = (int)(blockIdx.x >> 1);
+  const int m0 = (cid / n_tiles) * 256 + 128 * (int)rank;  // this CTA's rows of A and C
+  const int n0 = (cid % n_tiles) * 256;                    // the tile's columns
+  const int nb = n0 + HB * (int)rank;                              // this CTA's rows of B (N)
+  const int nk = (p.K + BK - 1) / BK;
+  const int nchunks = (nk + KC - 1) / KC;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; ++s) {
+      mbar_init(smem_u32(&full[s]), 1);
+      mbar_init(smem_u32(&empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&acc_full[b]), 1);
+      mbar_init(smem_u32(&acc_free[b]), 2 * EPI_WARPS);
+    }
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+  }
+  fence_before();
+  cluster_sync_all();
+  fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the leader's full[0]
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % STAGES2;
+        const uint32_t ph = (kb / STAGES2) & 1;
+        if (kb >= STAGES2 && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) break;
+        unsigned char* st = smem + s * STAGE2_BYTES;
+        const uint32_t sA = smem_u32(st), sAx = sA + A_TILE;
+        const uint32_t sB = sAx + A_TILE, sBx = sB + B_HALF;
+        const uint32_t fb = full0 + 8u * (uint32_t)s;
+        if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * STAGE2_BYTES);
+        const int k0 = kb * BK;
+        if (TA == 0) {
+          tma_load_2d_pair(sA, &tmA, fb, k0, m0);
+          if (!PAIR) tma_load_2d_pair(sAx, &tmAx, fb, k0, m0);
+        } else {
+#pragma unroll
+          for (int c = 0; c < BM / 32; ++c) {
+            tma_load_2d_pair(sA + c * 4096, &tmA, fb, m0 + 32 * c, k0);
+            if (!PAIR) tma_load_2d_pair(sAx + c * 4096, &tmAx, fb, m0 + 32 * c, k0);
+          }
+        }
+        if (TB == 1) {
+          tma_load_2d_pair(sB, &tmB, fb, k0, nb);
+          if (!PAIR) tma_load_2d_pair(sBx, &tmBx, fb, k0, nb);
+        } else {
+#pragma unroll
+          for (int c = 0; c < HB / 32; ++c) {
+            tma_load_2d_pair(sB + c * 4096, &tmB, fb, nb + 32 * c, k0);
+            if (!PAIR) tma_load_2d_pair(sBx + c * 4096, &tmBx, fb, nb + 32 * c, k0);
+          }
+        }
+        if (PAIR) {
+          tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
+          tma_load_2d_pair(sBx, &tmBx, fb, 2 * k0, nb);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // --------------------------------------------------------- MMA (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = idesc2_tf32<TA, TB ? 0 : 1>();
+      bool ok = true;
+      for (int c = 0; c < nchunks && ok; ++c) {
+        const int b = c & 1;
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        if (c >= 2 && !mbar_wait(smem_u32(&acc_free[b]), ((c >> 1) - 1) & 1)) break;
+        fence_after();
+        const int kb_end = min(nk, (c + 1) * KC);
+        for (int kb = c * KC; kb < kb_end; ++kb) {
+          const int s = kb % STAGES2;
+          const uint32_t ph = (kb / STAGES2) & 1;
+          if (!mbar_wait(smem_u32(&full[s]), ph)) {
+            ok = false;
+            break;
+          }
+          fence_after();
+          unsigned char* st = smem + s * STAGE2_BYTES;
+          const uint32_t sA = smem_u32(st), sAx = sA + A_TILE;
+          const uint32_t sB = sAx + A_TILE, sBx = sB + B_HALF;
+          if constexpr (PAIR) {
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma2_tf32(acc, a, bh, idesc, first);
+            }
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              mma2_bf16(acc, kmajor_desc(sAx, k), kmajor_desc(sBx, k), idesc2_bf16());
+          } else {
+#pragma unroll
+            for (int k = 0; k < BK / 8; ++k) {
+              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+              const uint64_t al = TA ? mnmajor_desc(sAx, k) : kmajor_desc(sAx, k);
+              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+              const uint64_t bl = TB ? kmajor_desc(sBx, k) : mnmajor_desc(sBx, k);
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma2_tf32(acc, a, bh, idesc, first);
+              mma2_tf32(acc, a, bl, idesc, 1u);
+              mma2_tf32(acc, al, bh, idesc, 1u);
+            }
+          }
+          mma2_commit_both(smem_u32(&empty[s]));  // frees stage s in both CTAs
+        }
+        mma2_commit_both(smem_u32(&acc_full[b]));  // chunk ready in both CTAs
+      }
+    }
+    __syncwarp();
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int e = warp - 2;
+    const int quarter = warp & 3;
+    const int half = e >= 4 ? 1 : 0;
+    const int row = m0 + quarter * 32 + lane;
+    const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
+    const uint32_t free0 = mapa_shared(smem_u32(&acc_free[0]), 0);  // the leader's acc_free[0]
+    float sum[BN / 2];
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) sum[j] = 0.f;
+    bool ok = true;
+    for (int c = 0; c < nchunks; ++c) {
+      const int b = c & 1;
+      if (!mbar_wait(smem_u32(&acc_full[b]), (c >> 1) & 1)) {
+        ok = false;
+        break;
+      }
+      fence_after();
+      __syncwarp();
+      const uint32_t base = tmem + lane_base + (uint32_t)(b * BN + half * (BN / 2));
+#pragma unroll
+      for (int q = 0; q < BN / 64; ++q) {
+        float v[32];
+        tmem_ld32(base + q * 32, v);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[q * 32 + j] = __fadd_rn(sum[q * 32 + j], v[j]);
+      }
+      fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
+    }
+    const int nb0 = n0 + half * (BN / 2);
+    if (ok && row < p.M && nb0 < p.N) {
+      if (p.bias) {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
+      }
+      if (p.epilogue == TL_EPI_RELU) {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
+      }
+      float* crow = p.C + (int64_t)row * p.ldc + nb0;
+      const bool vec_ok = (p.ldc % 4 == 0) && (((uintptr_t)p.C & 15) == 0) && nb0 + BN / 2 <= p.N;
+      if (vec_ok) {
+        float4* c4 = reinterpret_cast<float4*>(crow);
+#pragma unroll
+        for (int j = 0; j < BN / 8; ++j) {
+          float4 o = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+          if (p.accumulate) {
+            float4 q = c4[j];
+            o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
+          }
+          c4[j] = o;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < BN / 2; ++j)
+          if (nb0 + j < p.N) crow[j] = p.accumulate ? crow[j] + sum[j] : sum[j];
+      }
+    }
+  }
+  fence_before();
+  cluster_sync_all();  // neither CTA releases TMEM or exits while the pair is still working
+  if (warp == 1) {
+    fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
+                 : "memory");
+  }
+}
+
 __device__ __forceinline__ float tf32_rna(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -634,6 +938,26 @@ int workspace(size_t floats, float** out, cudaStream_t st) {
 
 int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both rounded
 int g_scheme = kSchemeTF32BF16;
+int g_cta_pair = 1;  // 256 x 256 CTA-pair tiles when the product has more than one row tile
+
+// Launch the single-CTA or the CTA-pair kernel over prepared tensor maps.
+template <int TA, int TB, int SCHEME>
+int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CUtensorMap& mb,
+              const CUtensorMap& mbx, const Params& p, int64_t M, int64_t N, cudaStream_t st) {
+  if (two) {
+    auto kern = gemm_tc2_kernel<TA, TB, SCHEME>;
+    TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES));
+    const int64_t clusters = ((M + 255) / 256) * ((N + 255) / 256);
+    if (2 * clusters > INT32_MAX) return TL_ERR_UNSUPPORTED;
+    kern<<<(unsigned)(2 * clusters), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, p);
+  } else {
+    auto kern = gemm_tc_kernel<TA, TB, SCHEME>;
+    TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
+    kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, max_, mb, mbx, p);
+  }
+  return after_launch();
+}
 
 unsigned split_grid(size_t n) {
   unsigned g = (unsigned)((n / 4 + 255) / 256);
@@ -670,17 +994,15 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
 
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
   const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
+  const bool two = g_cta_pair && M > BM;
+  const uint32_t b_box = two ? HB : BN;  // B rows a CTA loads per k-block (K-major B)
   CUtensorMap ma, map_, mb, mbp;
   if (!make_map(&ma, A, a_rows, a_cols, lda, 32, TA ? 32 : BM, TA == 1) ||
-      !make_map(&mb, B, b_rows, b_cols, ldb, 32, TB ? BN : 32, TB == 0) ||
-      !make_pair_map(&map_, ap, M, kp, BM) || !make_pair_map(&mbp, bp, N, kp, BN))
+      !make_map(&mb, B, b_rows, b_cols, ldb, 32, TB ? b_box : 32, TB == 0) ||
+      !make_pair_map(&map_, ap, M, kp, BM) || !make_pair_map(&mbp, bp, N, kp, b_box))
     return TL_ERR_UNSUPPORTED;
   Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
-  auto kern = gemm_tc_kernel<TA, TB, kSchemeTF32BF16>;
-  TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, map_, mb, mbp, p);
-  return after_launch();
+  return run_tiles<TA, TB, kSchemeTF32BF16>(two, ma, map_, mb, mbp, p, M, N, st);
 }
 
 template <int TA, int TB>
@@ -721,8 +1043,9 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
   }
 
   CUtensorMap ma, mal, mb, mbl;
+  const bool two = g_cta_pair && M > BM;
   const uint32_t a_inner = 32, a_outer = TA ? 32 : BM;
-  const uint32_t b_inner = 32, b_outer = TB ? BN : 32;
+  const uint32_t b_inner = 32, b_outer = TB ? (two ? HB : BN) : 32;
   const bool a_mn = TA == 1, b_mn = TB == 0;
   if (!make_map(&ma, a_hi, a_rows, a_cols, lda, a_inner, a_outer, a_mn) ||
       !make_map(&mal, a_lo, a_rows, a_cols, lda, a_inner, a_outer, a_mn) ||
@@ -730,11 +1053,7 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
       !make_map(&mbl, b_lo, b_rows, b_cols, ldb, b_inner, b_outer, b_mn))
     return TL_ERR_UNSUPPORTED;
   Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
-  auto kern = gemm_tc_kernel<TA, TB, kScheme3xTF32>;
-  TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-  dim3 grid((unsigned)((N + BN - 1) / BN), (unsigned)((M + BM - 1) / BM));
-  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ma, mal, mb, mbl, p);
-  return after_launch();
+  return run_tiles<TA, TB, kScheme3xTF32>(two, ma, mal, mb, mbl, p, M, N, st);
 }
 
 }  // namespace
@@ -767,6 +1086,12 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
 }
 
 void gemm_set_split_mode(int mode) { g_split_mode = mode; }
+
+int gemm_set_cta_pair(int enable) {
+  const int prev = g_cta_pair;
+  g_cta_pair = enable ? 1 : 0;
+  return prev;
+}
 
 int gemm_set_scheme(int scheme) {
   if (scheme != kScheme3xTF32 && scheme != kSchemeTF32BF16) return -1;

@@ -5,7 +5,9 @@ transposed, B as stored or transposed), ragged M/N/K (the tensor-core tiles
 are 128x256x32, so partial tiles exercise TMA zero fill and masked stores;
 K not a multiple of 32 exercises the zero columns of the bf16 pair
 matrices), bias, relu and accumulate, under the default TF32+bf16 operand
-scheme and the three-TF32 scheme.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
+scheme and the three-TF32 scheme, on 256 x 256 CTA-pair tiles (the default
+for more than 128 rows; rows and columns past M and N exercise a pair whose
+second CTA is wholly out of range) and on single-CTA tiles.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
 the split-TF32 product is expected near 1e-6.  Also checks which path a
 shape takes and that no kernel left a device error.
 """
@@ -116,6 +118,26 @@ def test_gemm_three_tf32_scheme(ta, tb, M, N, K):
     finally:
         tl.runtime.check(L.tl_gemm_set_scheme(prev.value, None))
     assert prev.value == 1, "TF32+bf16 is the default scheme"
+
+
+@pytest.mark.parametrize("scheme", [0, 1])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 200), (1024, 512, 512)])
+def test_gemm_single_cta_tiles(scheme, ta, tb, M, N, K):
+    """128 x 256 single-CTA tiles (the CTA-pair tiles switched off)."""
+    tl = load_backend()
+    L = tl.runtime.lib()
+    prev_pair, prev_scheme = ctypes.c_int(-1), ctypes.c_int(-1)
+    tl.runtime.check(L.tl_gemm_set_cta_pair(0, ctypes.byref(prev_pair)))
+    tl.runtime.check(L.tl_gemm_set_scheme(scheme, ctypes.byref(prev_scheme)))
+    try:
+        out, ref, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
+        assert err == 0 and path == 0
+        assert_close(out, ref, 1e-5, f"single-CTA {scheme} {ta}{tb} {M}x{N}x{K}")
+    finally:
+        tl.runtime.check(L.tl_gemm_set_cta_pair(prev_pair.value, None))
+        tl.runtime.check(L.tl_gemm_set_scheme(prev_scheme.value, None))
+    assert prev_pair.value == 1, "CTA-pair tiles are the default"
 
 
 def test_gemm_scheme_rejects_unknown():
