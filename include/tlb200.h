@@ -218,6 +218,16 @@ int  tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
              const float* A, int64_t lda, const float* B, int64_t ldb,
              float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
              void* stream);
+/* tl_gemm with a relu-mask epilogue (no reference counterpart: it fuses the
+ * relu VJP grad * (x > 0) -- autograd.py:540-544 -- into the GEMM that
+ * produces grad):  C (+)= epilogue(op(A) op(B) + bias) * (mask[m, n] > 0 ? 1 : 0),
+ * the product rounded to nearest as a separate multiply.  mask is [M][ldm]
+ * (ldm >= N) and may be null (then this is tl_gemm).  Every path of tl_gemm
+ * supports it. */
+int  tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+                    const float* A, int64_t lda, const float* B, int64_t ldb,
+                    float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
+                    const float* mask, int64_t ldm, void* stream);
 /* Which path tl_gemm would take (0 tensor-core, 1 CUDA-core) for this call. */
 int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                   const float* A, int64_t lda, const float* B, int64_t ldb,

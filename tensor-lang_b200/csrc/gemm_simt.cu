@@ -16,7 +16,7 @@ namespace tl {
 
 int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
             const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
-            int epilogue, cudaStream_t st);
+            int epilogue, const float* mask, int64_t ldm, cudaStream_t st);
 bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                 const float* B, int64_t ldb, const float* C, int64_t ldc);
 void gemm_set_split_mode(int mode);
@@ -24,7 +24,7 @@ int gemm_set_scheme(int scheme);
 int gemm_set_cta_pair(int enable);
 int gemm_small(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
-               int accumulate, int epilogue, cudaStream_t st);
+               int accumulate, int epilogue, const float* mask, int64_t ldm, cudaStream_t st);
 bool gemm_small_ok(int ta, int tb, int64_t M, int64_t N, int64_t K);
 
 namespace {
@@ -38,7 +38,8 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int64_t M, int64_t N, int64_
                                                     const float* __restrict__ B, int64_t ldb,
                                                     float* __restrict__ C, int64_t ldc,
                                                     const float* __restrict__ bias, int accumulate,
-                                                    int epilogue) {
+                                                    int epilogue, const float* __restrict__ mask,
+                                                    int64_t ldm) {
   __shared__ __align__(16) float As[2][BK][BM + 4];
   __shared__ __align__(16) float Bs[2][BK][BN + 4];
   const int t = threadIdx.x;
@@ -128,6 +129,7 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int64_t M, int64_t N, int64_
       float v = acc[i][j];
       if (bias) v += bias[n];
       if (epilogue == TL_EPI_RELU) v = fmaxf(0.f, v);
+      if (mask) v = __fmul_rn(v, mask[m * ldm + n] > 0.f ? 1.f : 0.f);
       float* c = C + m * ldc + n;
       *c = accumulate ? *c + v : v;
     }
@@ -138,11 +140,12 @@ __global__ void __launch_bounds__(256) sgemm_kernel(int64_t M, int64_t N, int64_
 
 int gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
               const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
-              int accumulate, int epilogue, cudaStream_t st) {
+              int accumulate, int epilogue, const float* mask, int64_t ldm, cudaStream_t st) {
   dim3 grid(ceil_div_u(N, BN), ceil_div_u(M, BM));
   if (grid.y > 65535) return TL_ERR_UNSUPPORTED;
 #define TL_SG(a, b) \
-  sgemm_kernel<a, b><<<grid, 256, 0, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue)
+  sgemm_kernel<a, b><<<grid, 256, 0, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, \
+                                           mask, ldm)
   if (!ta && !tb) TL_SG(0, 0);
   else if (!ta && tb) TL_SG(0, 1);
   else if (ta && !tb) TL_SG(1, 0);
@@ -155,22 +158,31 @@ int gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, i
 
 extern "C" {
 
-int tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
-            const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
-            int epilogue, void* stream) {
+int tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A,
+                   int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                   const float* bias, int accumulate, int epilogue, const float* mask,
+                   int64_t ldm, void* stream) {
   if (M <= 0 || N <= 0 || !C) return TL_ERR_INVALID_ARG;
   if (K > 0 && (!A || !B)) return TL_ERR_INVALID_ARG;
+  if (mask && ldm < N) return TL_ERR_INVALID_ARG;
   cudaStream_t st = tl::stream_or_default(stream);
   if (!tl::g_force_simt && tl::gemm_tc_ok(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc))
     return tl::gemm_tc(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
-                       epilogue, st);
+                       epilogue, mask, ldm, st);
   if (K > 0 && tl::gemm_small_ok(trans_a, trans_b, M, N, K)) {
     int s = tl::gemm_small(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
-                           epilogue, st);
+                           epilogue, mask, ldm, st);
     if (s != TL_ERR_UNSUPPORTED) return s;
   }
   return tl::gemm_simt(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
-                       epilogue, st);
+                       epilogue, mask, ldm, st);
+}
+
+int tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+            const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
+            int epilogue, void* stream) {
+  return tl_gemm_masked(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
+                        epilogue, nullptr, 0, stream);
 }
 
 int tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A,

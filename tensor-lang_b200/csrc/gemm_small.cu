@@ -16,7 +16,8 @@
 //   nt  C[M,N]  = A[M,K]   @ B[N,K]^T  K <= 32   one thread per column n,
 //                                                  B row in registers
 //
-// All accumulate in fp32 with FMA; epilogue: + bias[n], relu, accumulate.
+// All accumulate in fp32 with FMA; epilogue: + bias[n], relu, relu mask
+// (v * (mask[m, n] > 0)), accumulate.
 #include <mutex>
 #include <vector>
 
@@ -28,6 +29,12 @@ namespace {
 constexpr int SMALL = 32;
 
 bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+// relu-mask epilogue (tl_gemm_masked): v * (mask[m, n] > 0), as the relu VJP
+__device__ __forceinline__ float mask_of(float v, const float* mask, int64_t ldm, int64_t m,
+                                         int64_t n) {
+  return mask ? __fmul_rn(v, mask[m * ldm + n] > 0.f ? 1.f : 0.f) : v;
+}
 
 __device__ __forceinline__ float epi(float v, const float* bias, int64_t n, int relu) {
   if (bias) v += bias[n];
@@ -44,7 +51,7 @@ __global__ void __launch_bounds__(256) small_nn_kernel(int64_t M, int N, int64_t
                                                        const float* __restrict__ B, int64_t ldb,
                                                        float* __restrict__ C, int64_t ldc,
                                                        const float* __restrict__ bias,
-                                                       int accumulate, int relu) {
+                                                       int accumulate, int relu, const float* __restrict__ mask, int64_t ldm) {
   constexpr int KCH = NB <= 16 ? 512 : 256;  // <= 34 KB of static shared memory
   __shared__ float Bs[KCH][NB + 1];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -84,7 +91,7 @@ __global__ void __launch_bounds__(256) small_nn_kernel(int64_t M, int N, int64_t
       float v = warp_sum(acc[r][n]);
       if (lane == n && n < N && m < M) {
         float* c = C + m * ldc + n;
-        float o = epi(v, bias, n, relu);
+        float o = mask_of(epi(v, bias, n, relu), mask, ldm, m, n);
         *c = accumulate ? *c + o : o;
       }
     }
@@ -101,7 +108,7 @@ __global__ void __launch_bounds__(256) small_tn_kernel(int64_t M, int N, int64_t
                                                        const float* __restrict__ B, int64_t ldb,
                                                        float* __restrict__ C, int64_t ldc,
                                                        const float* __restrict__ bias,
-                                                       int accumulate, int relu,
+                                                       int accumulate, int relu, const float* __restrict__ mask, int64_t ldm,
                                                        unsigned* counters, float* partials) {
   constexpr int KT = 256;
   __shared__ float Bs[KT][NB];
@@ -154,7 +161,7 @@ __global__ void __launch_bounds__(256) small_tn_kernel(int64_t M, int N, int64_t
     for (int n = 0; n < NB; ++n) {
       if (n < N) {
         float* c = C + m * ldc + n;
-        float o = epi(tot[n], bias, n, relu);
+        float o = mask_of(epi(tot[n], bias, n, relu), mask, ldm, m, n);
         *c = accumulate ? *c + o : o;
       }
     }
@@ -171,7 +178,7 @@ __global__ void __launch_bounds__(256) small_nt_kernel(int64_t M, int64_t N, int
                                                        const float* __restrict__ B, int64_t ldb,
                                                        float* __restrict__ C, int64_t ldc,
                                                        const float* __restrict__ bias,
-                                                       int accumulate, int relu, int rows) {
+                                                       int accumulate, int relu, const float* __restrict__ mask, int64_t ldm, int rows) {
   extern __shared__ float As[];  // [rows][KB]
   const int64_t n = (int64_t)blockIdx.x * 256 + threadIdx.x;
   const int64_t m0 = (int64_t)blockIdx.y * rows;
@@ -192,6 +199,7 @@ __global__ void __launch_bounds__(256) small_nt_kernel(int64_t M, int64_t N, int
     for (int k = 0; k < KB; ++k) v = fmaf(As[r * KB + k], b[k], v);
     v += bn;
     if (relu) v = fmaxf(0.f, v);
+    v = mask_of(v, mask, ldm, m0 + r, n);
     float* c = C + (m0 + r) * ldc + n;
     *c = accumulate ? *c + v : v;
   }
@@ -209,7 +217,7 @@ __global__ void __launch_bounds__(256, 2) small_nn4_kernel(int64_t M, int N, int
                                                            const float* __restrict__ B, int64_t ldb,
                                                            float* __restrict__ C, int64_t ldc,
                                                            const float* __restrict__ bias,
-                                                           int accumulate, int relu) {
+                                                           int accumulate, int relu, const float* __restrict__ mask, int64_t ldm) {
   constexpr int KCH = NB <= 16 ? 512 : 256, LDT = KCH + 4;
   __shared__ __align__(16) float Bt[NB * LDT];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -254,7 +262,7 @@ __global__ void __launch_bounds__(256, 2) small_nn4_kernel(int64_t M, int N, int
       const float v = warp_sum(acc[r][n]);
       if (lane == n && n < N && m < M) {
         float* c = C + m * ldc + n;
-        const float o = epi(v, bias, n, relu);
+        const float o = mask_of(epi(v, bias, n, relu), mask, ldm, m, n);
         *c = accumulate ? *c + o : o;
       }
     }
@@ -274,7 +282,7 @@ __global__ void __launch_bounds__(32 * kNnpWarps, 1) small_nn4p_kernel(int64_t M
                                                             const float* __restrict__ B, int64_t ldb,
                                                             float* __restrict__ C, int64_t ldc,
                                                             const float* __restrict__ bias,
-                                                            int accumulate, int relu) {
+                                                            int accumulate, int relu, const float* __restrict__ mask, int64_t ldm) {
   extern __shared__ __align__(16) float Btp[];
   const int64_t ldt = K + 4;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -333,7 +341,7 @@ __global__ void __launch_bounds__(32 * kNnpWarps, 1) small_nn4p_kernel(int64_t M
         const float v = warp_sum(acc[r][n]);
         if (lane == n && n < N && m < M) {
           float* c = C + m * ldc + n;
-          const float o = epi(v, bias, n, relu);
+          const float o = mask_of(epi(v, bias, n, relu), mask, ldm, m, n);
           *c = accumulate ? *c + o : o;
         }
       }
@@ -353,7 +361,7 @@ __global__ void __launch_bounds__(256, 2) small_tn4_kernel(int64_t M, int N, int
                                                            const float* __restrict__ B, int64_t ldb,
                                                            float* __restrict__ C, int64_t ldc,
                                                            const float* __restrict__ bias,
-                                                           int accumulate, int relu,
+                                                           int accumulate, int relu, const float* __restrict__ mask, int64_t ldm,
                                                            unsigned* counters, float* partials) {
   constexpr int KT = NB <= 12 ? 512 : 256;
   __shared__ __align__(16) float Bs[KT * NB];
@@ -463,7 +471,7 @@ __global__ void __launch_bounds__(256, 2) small_tn4_kernel(int64_t M, int N, int
     float tot = 0.f;
     for (unsigned y = 0; y < gridDim.y; ++y) tot += __ldcg(&partials[((size_t)y * M + mm) * NB + n]);
     float* c = C + mm * ldc + n;
-    const float v = epi(tot, bias, n, relu);
+    const float v = mask_of(epi(tot, bias, n, relu), mask, ldm, mm, n);
     *c = accumulate ? *c + v : v;
   }
   if (threadIdx.x == 0) counters[blockIdx.x] = 0u;
@@ -480,7 +488,7 @@ __global__ void __launch_bounds__(256) small_nt4_kernel(int64_t M, int64_t N, in
                                                         const float* __restrict__ B, int64_t ldb,
                                                         float* __restrict__ C, int64_t ldc,
                                                         const float* __restrict__ bias,
-                                                        int accumulate, int relu, int rows) {
+                                                        int accumulate, int relu, const float* __restrict__ mask, int64_t ldm, int rows) {
   extern __shared__ __align__(16) float As4[];  // [rows][KB]
   const int64_t n = ((int64_t)blockIdx.x * 256 + threadIdx.x) * 4;
   const int64_t m0 = (int64_t)blockIdx.y * rows;
@@ -518,6 +526,7 @@ __global__ void __launch_bounds__(256) small_nt4_kernel(int64_t M, int64_t N, in
     for (int c = 0; c < 4; ++c) {
       v[c] += bn[c];
       if (relu) v[c] = fmaxf(0.f, v[c]);
+      v[c] = mask_of(v[c], mask, ldm, m0 + r, n + c);
     }
     float4* c4 = reinterpret_cast<float4*>(C + (m0 + r) * ldc + n);
     float4 o = make_float4(v[0], v[1], v[2], v[3]);
@@ -576,7 +585,7 @@ int dispatch_nb(int n, Args... args) {
 template <int NB>
 struct RunNN {
   static int run(int64_t M, int N, int64_t K, const float* A, int64_t lda, const float* B,
-                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu,
+                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu, const float* mask, int64_t ldm,
                  cudaStream_t st) {
     constexpr int RPW = NB <= 12 ? 4 : 2;
     const int64_t blocks = (M + 8 * RPW - 1) / (8 * RPW);
@@ -589,16 +598,16 @@ struct RunNN {
           TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
           const int64_t groups = (M + kNnpWarps * RPW - 1) / (kNnpWarps * RPW);
           const unsigned grid = (unsigned)(groups < sm_count() ? groups : sm_count());
-          kern<<<grid, 32 * kNnpWarps, smem, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu);
+          kern<<<grid, 32 * kNnpWarps, smem, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm);
           return after_launch();
         }
       }
       small_nn4_kernel<NB, RPW><<<(unsigned)blocks, 256, 0, st>>>(M, N, K, A, lda, B, ldb, C, ldc,
-                                                                  bias, acc, relu);
+                                                                  bias, acc, relu, mask, ldm);
       return after_launch();
     }
     small_nn_kernel<NB, RPW><<<(unsigned)blocks, 256, 0, st>>>(M, N, K, A, lda, B, ldb, C, ldc,
-                                                                bias, acc, relu);
+                                                                bias, acc, relu, mask, ldm);
     return after_launch();
   }
 };
@@ -606,10 +615,10 @@ struct RunNN {
 template <int NB>
 struct RunTN {
   static int run(int64_t M, int N, int64_t K, const float* A, int64_t lda, const float* B,
-                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu,
+                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu, const float* mask, int64_t ldm,
                  cudaStream_t st) {
     if constexpr (NB <= 16) {
-      if (M % 4 == 0 && lda % 4 == 0 && aligned16(A)) return run4(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, st);
+      if (M % 4 == 0 && lda % 4 == 0 && aligned16(A)) return run4(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm, st);
     }
     const unsigned gx = (unsigned)((M + 255) / 256);
     if (gx > 1024) return TL_ERR_UNSUPPORTED;
@@ -622,12 +631,12 @@ struct RunTN {
     void* ws = nullptr;
     TL_TRY(small_workspace(4096 + (size_t)gy * M * NB * 4, &ws, st));
     small_tn_kernel<NB><<<dim3(gx, gy), 256, 0, st>>>(M, N, K, chunk, A, lda, B, ldb, C, ldc, bias,
-                                                       acc, relu, (unsigned*)ws,
+                                                       acc, relu, mask, ldm, (unsigned*)ws,
                                                        (float*)((char*)ws + 4096));
     return after_launch();
   }
   static int run4(int64_t M, int N, int64_t K, const float* A, int64_t lda, const float* B,
-                  int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu,
+                  int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu, const float* mask, int64_t ldm,
                   cudaStream_t st) {
     const unsigned gx = (unsigned)((M + 127) / 128);
     if (gx > 1024) return TL_ERR_UNSUPPORTED;
@@ -641,7 +650,7 @@ struct RunTN {
     void* ws = nullptr;
     TL_TRY(small_workspace(4096 + (size_t)gy * M * NB * 4, &ws, st));
     small_tn4_kernel<NB><<<dim3(gx, gy), 256, 0, st>>>(M, N, K, chunk, A, lda, B, ldb, C, ldc, bias,
-                                                        acc, relu, (unsigned*)ws,
+                                                        acc, relu, mask, ldm, (unsigned*)ws,
                                                         (float*)((char*)ws + 4096));
     return after_launch();
   }
@@ -650,7 +659,7 @@ struct RunTN {
 template <int KB>
 struct RunNT {
   static int run(int64_t M, int64_t N, int K, const float* A, int64_t lda, const float* B,
-                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu,
+                 int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu, const float* mask, int64_t ldm,
                  cudaStream_t st) {
     const int rows = 64;
     if constexpr (KB <= 16) {
@@ -658,27 +667,27 @@ struct RunNT {
       if (N % 4 == 0 && ldc % 4 == 0 && aligned16(C) && gy4 <= 65535) {
         const unsigned gx4 = (unsigned)((N + 1023) / 1024);
         small_nt4_kernel<KB><<<dim3(gx4, (unsigned)gy4), 256, rows * KB * 4, st>>>(
-            M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, rows);
+            M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm, rows);
         return after_launch();
       }
     }
     const unsigned gx = (unsigned)((N + 255) / 256);
     const int64_t gy = (M + rows - 1) / rows;
-    if (gy > 65535) return small_nt_launch_wide(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, st);
+    if (gy > 65535) return small_nt_launch_wide(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm, st);
     small_nt_kernel<KB><<<dim3(gx, (unsigned)gy), 256, rows * KB * 4, st>>>(
-        M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, rows);
+        M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm, rows);
     return after_launch();
   }
   // very tall outputs: more rows per block so the grid's y extent fits
   static int small_nt_launch_wide(int64_t M, int64_t N, int K, const float* A, int64_t lda,
                                   const float* B, int64_t ldb, float* C, int64_t ldc,
-                                  const float* bias, int acc, int relu, cudaStream_t st) {
+                                  const float* bias, int acc, int relu, const float* mask, int64_t ldm, cudaStream_t st) {
     const int64_t rows = (M + 65534) / 65535;
     if (rows * KB * 4 > 48 * 1024) return TL_ERR_UNSUPPORTED;
     const unsigned gx = (unsigned)((N + 255) / 256);
     const unsigned gy = (unsigned)((M + rows - 1) / rows);
     small_nt_kernel<KB><<<dim3(gx, gy), 256, (size_t)rows * KB * 4, st>>>(
-        M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, (int)rows);
+        M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm, (int)rows);
     return after_launch();
   }
 };
@@ -688,14 +697,17 @@ struct RunNT {
 // Returns TL_ERR_UNSUPPORTED when no skinny kernel applies.
 int gemm_small(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
-               int accumulate, int epilogue, cudaStream_t st) {
+               int accumulate, int epilogue, const float* mask, int64_t ldm, cudaStream_t st) {
   const int relu = epilogue == TL_EPI_RELU;
   if (N <= SMALL && !ta && !tb)
-    return dispatch_nb<RunNN>((int)N, M, (int)N, K, A, lda, B, ldb, C, ldc, bias, accumulate, relu, st);
+    return dispatch_nb<RunNN>((int)N, M, (int)N, K, A, lda, B, ldb, C, ldc, bias, accumulate, relu,
+                              mask, ldm, st);
   if (N <= SMALL && ta && !tb)
-    return dispatch_nb<RunTN>((int)N, M, (int)N, K, A, lda, B, ldb, C, ldc, bias, accumulate, relu, st);
+    return dispatch_nb<RunTN>((int)N, M, (int)N, K, A, lda, B, ldb, C, ldc, bias, accumulate, relu,
+                              mask, ldm, st);
   if (K <= SMALL && !ta && tb)
-    return dispatch_nb<RunNT>((int)K, M, N, (int)K, A, lda, B, ldb, C, ldc, bias, accumulate, relu, st);
+    return dispatch_nb<RunNT>((int)K, M, N, (int)K, A, lda, B, ldb, C, ldc, bias, accumulate, relu,
+                              mask, ldm, st);
   return TL_ERR_UNSUPPORTED;
 }
 

@@ -15,9 +15,11 @@
 // The TF32+bf16 scheme (the default) keeps hi*hi on the TF32 path and folds
 // both correction terms into one bf16 MMA over a K-concatenated pair:
 //   [bf16(A) | bf16(loA)] . [bf16(loB) | bf16(B)]  =  A*loB + loA*B  (+ ~2^-19)
-// A pre-pass writes each operand's pair tile K-major (transposing MN-major
-// operands), 32 values then 32 lows per 32-deep k-block, so one 128-byte
-// swizzled bf16 row holds a k-block's pair.  Per 8-deep k-step this is one
+// A pre-pass writes each operand's pair matrix in the operand's own major
+// order: for a K-major operand 32 values then 32 lows per 32-deep k-block
+// along each row (one 128-byte swizzled row holds a k-block's pair); for an
+// MN-major operand 32 rows of values then 32 rows of lows per k-block, each
+// row spanning M or N (64-wide MN-major boxes) -- no transpose.  Per 8-deep k-step this is one
 // TF32 MMA plus half a bf16 MMA of the same shape: 2 TF32 MMA-times instead of
 // 3.  Per product the error is below 9 * 2^-20 relative (lo*lo dropped,
 // bf16 rounding of the correction operands).
@@ -199,13 +201,31 @@ __host__ __device__ constexpr uint32_t idesc_tf32() {
          | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
 }
 
-// Instruction descriptor: kind::f16 with bf16 A and B (both K-major), fp32
-// accumulate, M=128, N=BN.
+// Instruction descriptor: kind::f16 with bf16 A and B, fp32 accumulate,
+// M=128, N=BN; A_MN / B_MN = 1 for an MN-major operand.
+template <int A_MN, int B_MN>
 __host__ __device__ constexpr uint32_t idesc_bf16() {
   return (1u << 4)     // D format: f32
          | (1u << 7)   // A format: bf16
          | (1u << 10)  // B format: bf16
-         | ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+         | ((uint32_t)A_MN << 15) | ((uint32_t)B_MN << 16) |
+         ((uint32_t)(BN >> 3) << 17) | ((uint32_t)(BM >> 4) << 24);
+}
+
+// MN-major bf16 pair tile: 64-wide chunks (128 B per pair row, 128-byte
+// swizzle) of 64 pair rows, 8 KB apart; 8-row groups 1 KB apart; one 16-deep
+// k-step is 16 rows = 2 KB.
+constexpr int PAIR_MN_CHUNK = 64 * 64 * 2;
+constexpr uint32_t kLayoutSW128Pair = 2;
+__device__ __forceinline__ uint64_t mn16_desc(uint32_t tile, int k) {
+  uint64_t d = 0;
+  const uint32_t saddr = tile + 2048u * (uint32_t)k;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((PAIR_MN_CHUNK >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((1024 >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)kLayoutSW128Pair << 61;
+  return d;
 }
 
 // Operand schemes
@@ -219,7 +239,59 @@ struct Params {
   const float* bias;
   int accumulate;
   int epilogue;
+  const float* mask;  // relu-mask epilogue: C = v * (mask > 0), or null
+  int64_t ldm;
 };
+
+// Epilogue of one thread's BN/2 columns of row `row` (bias, relu, relu mask,
+// accumulate, store); shared by the single-CTA and CTA-pair kernels.
+__device__ __forceinline__ void store_row(const Params& p, int row, int nb0, float (&sum)[BN / 2]) {
+  if (row >= p.M || nb0 >= p.N) return;
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j)
+      if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
+  }
+  if (p.epilogue == TL_EPI_RELU) {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
+  }
+  const bool full = nb0 + BN / 2 <= p.N;
+  if (p.mask) {
+    const float* mrow = p.mask + (int64_t)row * p.ldm + nb0;
+    if (full && (p.ldm % 4 == 0) && (((uintptr_t)p.mask & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < BN / 8; ++j) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(mrow) + j);
+        sum[4 * j] = __fmul_rn(sum[4 * j], q.x > 0.f ? 1.f : 0.f);
+        sum[4 * j + 1] = __fmul_rn(sum[4 * j + 1], q.y > 0.f ? 1.f : 0.f);
+        sum[4 * j + 2] = __fmul_rn(sum[4 * j + 2], q.z > 0.f ? 1.f : 0.f);
+        sum[4 * j + 3] = __fmul_rn(sum[4 * j + 3], q.w > 0.f ? 1.f : 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < BN / 2; ++j)
+        if (nb0 + j < p.N) sum[j] = __fmul_rn(sum[j], mrow[j] > 0.f ? 1.f : 0.f);
+    }
+  }
+  float* crow = p.C + (int64_t)row * p.ldc + nb0;
+  if (full && (p.ldc % 4 == 0) && (((uintptr_t)p.C & 15) == 0)) {
+    float4* c4 = reinterpret_cast<float4*>(crow);
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j) {
+      float4 o = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
+      if (p.accumulate) {
+        float4 q = c4[j];
+        o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
+      }
+      c4[j] = o;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j)
+      if (nb0 + j < p.N) crow[j] = p.accumulate ? crow[j] + sum[j] : sum[j];
+  }
+}
 
 // TA: 0 = A stored [M][K] (K-major), 1 = A stored [K][M] (MN-major)
 // TB: 0 = B stored [K][N] (MN-major), 1 = B stored [N][K] (K-major)
@@ -310,9 +382,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!PAIR) tma_load_2d(sBl + c * 4096, &tmBlo, fb, n0 + 32 * c, k0);
           }
         }
-        if (PAIR) {  // k-block kb of the pair matrices starts at column 64*kb = 2*k0
-          tma_load_2d(sAl, &tmAlo, fb, 2 * k0, m0);
-          tma_load_2d(sBl, &tmBlo, fb, 2 * k0, n0);
+        if (PAIR) {  // k-block kb of the pair matrices starts at pair index 64*kb = 2*k0
+          if (TA == 0) {
+            tma_load_2d(sAl, &tmAlo, fb, 2 * k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_2d(sAl + c * PAIR_MN_CHUNK, &tmAlo, fb, m0 + 64 * c, 2 * k0);
+          }
+          if (TB == 1) {
+            tma_load_2d(sBl, &tmBlo, fb, 2 * k0, n0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BN / 64; ++c)
+              tma_load_2d(sBl + c * PAIR_MN_CHUNK, &tmBlo, fb, n0 + 64 * c, 2 * k0);
+          }
         }
       }
     }
@@ -350,7 +434,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             // 64 bf16 per row (32 values, 32 lows): 4 k-steps of 16, each a 32-byte advance
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma_bf16(acc, kmajor_desc(sAl, k), kmajor_desc(sBl, k), idesc_bf16());
+              mma_bf16(acc, TA ? mn16_desc(sAl, k) : kmajor_desc(sAl, k),
+                       TB ? kmajor_desc(sBl, k) : mn16_desc(sBl, k), idesc_bf16<TA, TB ? 0 : 1>());
           } else {
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k) {
@@ -401,36 +486,7 @@ __global__ void __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(&acc_free[b])) : "memory");
     }
-    const int nb0 = n0 + half * (BN / 2);
-    if (ok && row < p.M && nb0 < p.N) {
-      if (p.bias) {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j)
-          if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
-      }
-      if (p.epilogue == TL_EPI_RELU) {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
-      }
-      float* crow = p.C + (int64_t)row * p.ldc + nb0;
-      const bool vec_ok = (p.ldc % 4 == 0) && (((uintptr_t)p.C & 15) == 0) && nb0 + BN / 2 <= p.N;
-      if (vec_ok) {
-        float4* c4 = reinterpret_cast<float4*>(crow);
-#pragma unroll
-        for (int j = 0; j < BN / 8; ++j) {
-          float4 o = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
-          if (p.accumulate) {
-            float4 q = c4[j];
-            o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
-          }
-          c4[j] = o;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j)
-          if (nb0 + j < p.N) crow[j] = p.accumulate ? crow[j] + sum[j] : sum[j];
-      }
-    }
+    if (ok) store_row(p, row, n0 + half * (BN / 2), sum);
   }
   fence_before();
   __syncthreads();
@@ -520,9 +576,10 @@ __host__ __device__ constexpr uint32_t idesc2_tf32() {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)A_MN << 15) | ((uint32_t)B_MN << 16) |
          ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
+template <int A_MN, int B_MN>
 __host__ __device__ constexpr uint32_t idesc2_bf16() {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(256 >> 3) << 17) |
-         ((uint32_t)(256 >> 4) << 24);
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)A_MN << 15) | ((uint32_t)B_MN << 16) |
+         ((uint32_t)(256 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
 }
 
 template <int TA, int TB, int SCHEME>
@@ -611,8 +668,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
         }
         if (PAIR) {
-          tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
-          tma_load_2d_pair(sBx, &tmBx, fb, 2 * k0, nb);
+          if (TA == 0) {
+            tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
+          } else {
+#pragma unroll
+            for (int c = 0; c < BM / 64; ++c)
+              tma_load_2d_pair(sAx + c * PAIR_MN_CHUNK, &tmAx, fb, m0 + 64 * c, 2 * k0);
+          }
+          if (TB == 1) {
+            tma_load_2d_pair(sBx, &tmBx, fb, 2 * k0, nb);
+          } else {
+#pragma unroll
+            for (int c = 0; c < HB / 64; ++c)
+              tma_load_2d_pair(sBx + c * PAIR_MN_CHUNK, &tmBx, fb, nb + 64 * c, 2 * k0);
+          }
         }
       }
     }
@@ -649,7 +718,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             }
 #pragma unroll
             for (int k = 0; k < 4; ++k)
-              mma2_bf16(acc, kmajor_desc(sAx, k), kmajor_desc(sBx, k), idesc2_bf16());
+              mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
+                        TB ? kmajor_desc(sBx, k) : mn16_desc(sBx, k), idesc2_bf16<TA, TB ? 0 : 1>());
           } else {
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k) {
@@ -701,36 +771,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
     }
-    const int nb0 = n0 + half * (BN / 2);
-    if (ok && row < p.M && nb0 < p.N) {
-      if (p.bias) {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j)
-          if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
-      }
-      if (p.epilogue == TL_EPI_RELU) {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
-      }
-      float* crow = p.C + (int64_t)row * p.ldc + nb0;
-      const bool vec_ok = (p.ldc % 4 == 0) && (((uintptr_t)p.C & 15) == 0) && nb0 + BN / 2 <= p.N;
-      if (vec_ok) {
-        float4* c4 = reinterpret_cast<float4*>(crow);
-#pragma unroll
-        for (int j = 0; j < BN / 8; ++j) {
-          float4 o = make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]);
-          if (p.accumulate) {
-            float4 q = c4[j];
-            o.x += q.x; o.y += q.y; o.z += q.z; o.w += q.w;
-          }
-          c4[j] = o;
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < BN / 2; ++j)
-          if (nb0 + j < p.N) crow[j] = p.accumulate ? crow[j] + sum[j] : sum[j];
-      }
-    }
+    if (ok) store_row(p, row, n0 + half * (BN / 2), sum);
   }
   fence_before();
   cluster_sync_all();  // neither CTA releases TMEM or exits while the pair is still working
@@ -819,43 +860,38 @@ __global__ void __launch_bounds__(256) pair_rows_kernel(const float* __restrict_
   }
 }
 
-// Pair matrix of an MN-major operand (X stored [K][R], X_eff[r][k] = X[k*ld + r]):
-// a 32 (k) x 128 (r) tile is staged in shared memory (odd row pitch:
-// conflict-free both ways) and written as 128 rows of one 128-byte k-block.
-__global__ void __launch_bounds__(256) pair_cols_kernel(const float* __restrict__ X, int64_t ld,
-                                                        int64_t R, int64_t K, int64_t kp,
-                                                        int lo_first, __nv_bfloat16* __restrict__ P) {
-  __shared__ float S[32][129];
-  const int64_t nrt = (R + 127) / 128, nkb = kp / 32;
-  for (int64_t t = blockIdx.x; t < nrt * nkb; t += gridDim.x) {
-    const int64_t rt = t % nrt, j = t / nrt;
-    const int64_t r0 = rt * 128, k0 = j * 32;
-    __syncthreads();
-#pragma unroll 4
-    for (int e = threadIdx.x; e < 32 * 128; e += 256) {
-      const int kk = e >> 7, rr = e & 127;
-      const int64_t k = k0 + kk, r = r0 + rr;
-      S[kk][rr] = (k < K && r < R) ? X[k * ld + r] : 0.f;
-    }
-    __syncthreads();
+// Pair matrix of an MN-major operand, kept MN-major (X stored [K][R], row
+// stride ld): pair row 64j+i holds bf16 of X[32j+i][0..R) and pair row
+// 64j+32+i bf16 of lo(X[32j+i][...]) -- the other way round when lo_first --
+// in rows of rp (R rounded up to 8) elements.  Rows for k >= K and columns
+// r >= R are zero.  A streaming map: each thread converts 8 consecutive r of
+// one k row.
+__global__ void __launch_bounds__(256) pair_mn_kernel(const float* __restrict__ X, int64_t ld,
+                                                      int64_t K, int64_t R, int64_t rp, int64_t kp,
+                                                      int lo_first, __nv_bfloat16* __restrict__ P) {
+  const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
+  const int64_t ng = rp >> 3;
+  for (int64_t k = blockIdx.x; k < kp; k += gridDim.x) {
+    const float* src = X + k * ld;
+    __nv_bfloat16* vrow = P + (64 * (k >> 5) + (k & 31)) * rp;
+    __nv_bfloat16* lrow = vrow + 32 * rp;
+    for (int64_t g = threadIdx.x; g < ng; g += blockDim.x) {
+      const int64_t r = 8 * g;
+      float x[8];
+      if (k < K && vec && r + 7 < R) {
+        const float4 a = ld_stream4(src + r), b = ld_stream4(src + r + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      } else {
 #pragma unroll
-    for (int c = threadIdx.x; c < 128 * 8; c += 256) {
-      const int rr = c >> 3, part = c & 7;  // 8 chunks of 16 bytes per output row
-      const int64_t r = r0 + rr;
-      if (r >= R) continue;
-      const int h = part >> 2, kk0 = (part & 3) * 8;
-      const bool low = (h == 0) == (lo_first != 0);
-      uint32_t w[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float x0 = S[kk0 + 2 * i][rr], x1 = S[kk0 + 2 * i + 1][rr];
-        if (low) {
-          x0 = lo_of(x0);
-          x1 = lo_of(x1);
-        }
-        w[i] = pack_bf16(x0, x1);
+        for (int i = 0; i < 8; ++i) x[i] = (k < K && r + i < R) ? src[r + i] : 0.f;
       }
-      *reinterpret_cast<uint4*>(P + r * 2 * kp + 64 * j + 32 * h + kk0) = make_uint4(w[0], w[1], w[2], w[3]);
+      const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
+                                  pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])),
+                                  pack_bf16(lo_of(x[4]), lo_of(x[5])), pack_bf16(lo_of(x[6]), lo_of(x[7])));
+      *reinterpret_cast<uint4*>(vrow + r) = lo_first ? lv : hv;
+      *reinterpret_cast<uint4*>(lrow + r) = lo_first ? hv : lv;
     }
   }
 }
@@ -907,6 +943,18 @@ bool make_pair_map(CUtensorMap* m, const __nv_bfloat16* base, int64_t rows, int6
   cuuint64_t dims[2] = {(cuuint64_t)(2 * kp), (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)(2 * kp) * 2};
   cuuint32_t box[2] = {64, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// 2-D bf16 tensor map over an MN-major pair matrix [2*kp][rp]: 64 x 64 boxes
+// (128 B rows), 128-byte swizzle.
+bool make_pair_map_mn(CUtensorMap* m, const __nv_bfloat16* base, int64_t rp, int64_t kp) {
+  cuuint64_t dims[2] = {(cuuint64_t)rp, (cuuint64_t)(2 * kp)};
+  cuuint64_t strides[1] = {(cuuint64_t)rp * 2};
+  cuuint32_t box[2] = {64, 64};
   cuuint32_t estr[2] = {1, 1};
   return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, (void*)base, dims, strides, box, estr,
                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -973,10 +1021,12 @@ unsigned pair_grid(int64_t units) {
 template <int TA, int TB>
 int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B,
                 int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
-                cudaStream_t st) {
+                const float* mask, int64_t ldm, cudaStream_t st) {
   const int64_t kp = (K + 31) / 32 * 32;
-  const size_t a_bytes = ((size_t)M * kp * 4 + 1023) / 1024 * 1024;  // [M][2kp] bf16
-  const size_t b_bytes = ((size_t)N * kp * 4 + 1023) / 1024 * 1024;
+  const int64_t mp = (M + 7) / 8 * 8, np_ = (N + 7) / 8 * 8;  // MN-major pair row lengths
+  // K-major pairs: [M][2kp]; MN-major pairs: [2kp][mp] (bf16, 4 bytes per element pair)
+  const size_t a_bytes = ((size_t)(TA ? mp : M) * kp * 4 + 1023) / 1024 * 1024;
+  const size_t b_bytes = ((size_t)(TB ? N : np_) * kp * 4 + 1023) / 1024 * 1024;
   float* ws = nullptr;
   TL_TRY(workspace((a_bytes + b_bytes) / 4, &ws, st));
   __nv_bfloat16* ap = reinterpret_cast<__nv_bfloat16*>(ws);
@@ -984,12 +1034,12 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
   if (TA == 0)
     pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, ap);
   else
-    pair_cols_kernel<<<pair_grid((M + 127) / 128 * (kp / 32)), 256, 0, st>>>(A, lda, M, K, kp, 0, ap);
+    pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(A, lda, K, M, mp, kp, 0, ap);
   TL_TRY(after_launch());
   if (TB == 1)
     pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, bp);
   else
-    pair_cols_kernel<<<pair_grid((N + 127) / 128 * (kp / 32)), 256, 0, st>>>(B, ldb, N, K, kp, 1, bp);
+    pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(B, ldb, K, N, np_, kp, 1, bp);
   TL_TRY(after_launch());
 
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
@@ -999,18 +1049,21 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
   CUtensorMap ma, map_, mb, mbp;
   if (!make_map(&ma, A, a_rows, a_cols, lda, 32, TA ? 32 : BM, TA == 1) ||
       !make_map(&mb, B, b_rows, b_cols, ldb, 32, TB ? b_box : 32, TB == 0) ||
-      !make_pair_map(&map_, ap, M, kp, BM) || !make_pair_map(&mbp, bp, N, kp, b_box))
+      !(TA ? make_pair_map_mn(&map_, ap, mp, kp) : make_pair_map(&map_, ap, M, kp, BM)) ||
+      !(TB ? make_pair_map(&mbp, bp, N, kp, b_box) : make_pair_map_mn(&mbp, bp, np_, kp)))
     return TL_ERR_UNSUPPORTED;
-  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm};
   return run_tiles<TA, TB, kSchemeTF32BF16>(two, ma, map_, mb, mbp, p, M, N, st);
 }
 
 template <int TA, int TB>
 int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
-           float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, cudaStream_t st) {
+           float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, const float* mask,
+           int64_t ldm, cudaStream_t st) {
   if (!load_encode()) return TL_ERR_UNSUPPORTED;
   if (g_scheme == kSchemeTF32BF16 && g_split_mode == 0)
-    return launch_pair<TA, TB>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+    return launch_pair<TA, TB>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask,
+                               ldm, st);
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
   const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
   // the elements a row-major [rows][cols] matrix with leading dim ld spans
@@ -1052,7 +1105,7 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
       !make_map(&mb, b_hi, b_rows, b_cols, ldb, b_inner, b_outer, b_mn) ||
       !make_map(&mbl, b_lo, b_rows, b_cols, ldb, b_inner, b_outer, b_mn))
     return TL_ERR_UNSUPPORTED;
-  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue};
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm};
   return run_tiles<TA, TB, kScheme3xTF32>(two, ma, mal, mb, mbl, p, M, N, st);
 }
 
@@ -1078,11 +1131,14 @@ bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A,
 
 int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
             const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
-            int epilogue, cudaStream_t st) {
-  if (!ta && !tb) return launch<0, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
-  if (!ta && tb) return launch<0, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
-  if (ta && !tb) return launch<1, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
-  return launch<1, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, st);
+            int epilogue, const float* mask, int64_t ldm, cudaStream_t st) {
+  if (!ta && !tb)
+    return launch<0, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
+  if (!ta && tb)
+    return launch<0, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
+  if (ta && !tb)
+    return launch<1, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
+  return launch<1, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
 }
 
 void gemm_set_split_mode(int mode) { g_split_mode = mode; }

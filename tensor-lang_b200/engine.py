@@ -28,6 +28,7 @@ import numpy as np
 
 from . import runtime as rt
 from .autograd import BackwardPlanner, Node, grad_name
+from .epilogue import fuse_gemm_epilogues
 from .kernel_generator import KernelGenerator
 from .shapes import Shape, broadcast, complete_env, expr_inputs, numel
 from .steps import EW, Copy, LibCall, Memset0, RegionStep, Step, fuse, kinfo_to_step
@@ -407,6 +408,8 @@ class Program:
         return out
 
     def _fuse_all(self):
+        if self.fuse_ops:
+            fuse_gemm_epilogues(self)
         live = set(self.shapes) if self.fetch is None else set(self.fetch)
         live |= set(self.initial)
         live |= {sv["tensor"] for sv in self.saves}

@@ -103,6 +103,9 @@ _SIGS = [
     ("tl_concat_rows", c_int, [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_void_p]),
     ("tl_gemm", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                         c_int64, c_void_p, c_int64, c_void_p, c_int, c_int, c_void_p]),
+    ("tl_gemm_masked", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                               c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int,
+                               c_void_p, c_int64, c_void_p]),
     ("tl_gemm_path", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                              c_int64, c_void_p, c_int64]),
     ("tl_gemm_force_simt", c_int, [c_int]),

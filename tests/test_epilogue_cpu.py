@@ -1,0 +1,77 @@
+"""The GEMM epilogue fusion pass (tensor-lang_b200/epilogue.py) on lowered
+programs, on the CPU: which rewrites apply, and which are blocked.
+
+The numerics of the rewritten programs are checked on the GPU
+(test_gpu_epilogue.py: bit-identical to the unfused program)."""
+from conftest import load_backend
+
+load_backend()  # registers the package as tensor_lang_b200
+
+
+def _mlp3(fetch, **kw):
+    tl = load_backend()
+    pr = tl.programs
+    ast = pr.mlp3_train(B=64, I=32, H=48, C=10, epochs=2)
+    return tl.Program(ast, None, feeds=pr.mlp3_inputs(B=64, I=32, H=48, C=10), fetch=fetch, **kw)
+
+
+def _steps(P):
+    from tensor_lang_b200.epilogue import _flat
+    return [s for _, s in _flat(P)]
+
+
+def _opcodes(P):
+    return [getattr(s, "opcode", None) for s in _steps(P)]
+
+
+def test_mlp3_relu_and_mask_fold_into_gemms():
+    from tensor_lang_b200.epilogue import fuse_gemm_epilogues
+    P = _mlp3(["loss", "W3"])
+    assert fuse_gemm_epilogues(P) == 6
+    ops = _opcodes(P)
+    assert "relu" not in ops and "relu_mask" not in ops
+    steps = _steps(P)
+    masked = [s for s in steps if getattr(s, "fname", "") == "tl_gemm_masked"]
+    assert sorted(s.writes[0] for s in masked) == ["h1_grad", "h2_grad"]
+    assert sorted(s.args[14][1] for s in masked) == ["a1", "a2"]   # masks: the relu outputs
+    relu_gemms = [s for s in steps if getattr(s, "fname", "") == "tl_gemm" and s.args[13] == ("int", 1)]
+    assert sorted(s.writes[0] for s in relu_gemms) == ["a1", "a2"]
+    names = {n for s in steps for n in s.reads + s.writes}
+    assert "h1" not in names and "h2" not in names      # pre-activations never materialised
+
+
+def test_nothing_fuses_when_every_tensor_is_fetched():
+    from tensor_lang_b200.epilogue import fuse_gemm_epilogues
+    P = _mlp3(None)
+    assert fuse_gemm_epilogues(P) == 0
+    assert _opcodes(P).count("relu") == 2
+
+
+def test_fetched_pre_activation_keeps_its_relu():
+    from tensor_lang_b200.epilogue import fuse_gemm_epilogues
+    P = _mlp3(["loss", "h1"])
+    fuse_gemm_epilogues(P)
+    steps = _steps(P)
+    assert any(getattr(s, "opcode", None) == "relu" and s.reads == ["h1"] for s in steps)
+    assert any("h1" in s.writes for s in steps)
+    # the second layer still folds
+    assert not any(getattr(s, "opcode", None) == "relu" and s.reads == ["h2"] for s in steps)
+
+
+def test_second_reader_blocks_relu_fold():
+    tl = load_backend()
+    pr = tl.programs
+    L, C, F = pr._let, pr._call, pr._fill
+    ast = [L("x", F((8, 16)), (8, 16)), L("W", F((16, 32)), (16, 32)), L("b", F((32,)), (32,)),
+           L("h", C("linear", "x", "W", "b")), L("a", C("relu", "h")),
+           L("s", {"type": "sum", "tensor": "h", "axis": 1})]
+    from tensor_lang_b200.epilogue import fuse_gemm_epilogues
+    P = tl.Program(ast, None, fetch=["a", "s"])
+    assert fuse_gemm_epilogues(P) == 0
+
+
+def test_engine_runs_the_pass_only_with_fusion_on():
+    for fuse_ops, masked in ((False, 0), (True, 2)):
+        P = _mlp3(["loss", "W3"], fuse_ops=fuse_ops)
+        P._fuse_all()
+        assert sum(getattr(s, "fname", "") == "tl_gemm_masked" for s in _steps(P)) == masked

@@ -1,0 +1,88 @@
+"""GEMM epilogues on the GPU: the relu-mask epilogue (tl_gemm_masked) on every
+GEMM path against a float64 product, and a training program whose relu and
+relu-VJP passes were folded into GEMM epilogues against the same program run
+unfused -- bit-identical, since the folded ops round exactly as the region
+kernels do.  Tolerance for the products: rel 1e-5 of max|C|."""
+import ctypes
+
+import numpy as np
+import pytest
+
+from conftest import assert_close, load_backend
+
+pytestmark = pytest.mark.gpu
+
+
+def _masked(ta, tb, M, N, K, bias=False, acc=False, relu=False, seed=0):
+    tl = load_backend()
+    rt = tl.runtime
+    L = rt.lib()
+    dev = rt.Device.get(0)
+    rng = np.random.default_rng(seed + M + 3 * N + 7 * K)
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    C0 = rng.standard_normal((M, N)).astype(np.float32)
+    bv = rng.standard_normal(N).astype(np.float32)
+    mask = rng.standard_normal((M, N)).astype(np.float32)
+    mask[rng.random((M, N)) < 0.1] = 0.0          # exact zeros are masked out
+    mask[0, : min(N, 4)] = [np.nan, -0.0, np.inf, -np.inf][: min(N, 4)]
+    bufs = [rt.DeviceBuffer(dev, a.shape) for a in (A, B, C0, bv, mask)]
+    for b, a in zip(bufs, (A, B, C0, bv, mask)):
+        b.upload(a)
+    dA, dB, dC, db, dm = bufs
+    rt.check(L.tl_gemm_masked(ta, tb, M, N, K, dA.ptr, A.shape[1], dB.ptr, B.shape[1], dC.ptr, N,
+                              db.ptr if bias else None, 1 if acc else 0, 1 if relu else 0,
+                              dm.ptr, N, dev.stream))
+    out = dC.download()
+    err = ctypes.c_int(0)
+    rt.check(L.tl_device_error(ctypes.byref(err), 1))
+    for b in bufs:
+        b.free()
+    Am = A.astype(np.float64).T if ta else A.astype(np.float64)
+    Bm = B.astype(np.float64).T if tb else B.astype(np.float64)
+    ref = Am @ Bm
+    if bias:
+        ref = ref + bv
+    if relu:
+        ref = np.maximum(ref, 0)
+    ref = ref * (mask > 0)
+    if acc:
+        ref = ref + C0
+    return out, ref, err.value
+
+
+@pytest.mark.parametrize("ta,tb,M,N,K", [
+    (0, 0, 300, 520, 200),     # tensor cores, CTA pair
+    (0, 1, 1024, 512, 512),
+    (1, 0, 640, 256, 300),
+    (1, 1, 100, 300, 64),      # tensor cores, single CTA (M <= 128)
+    (0, 0, 1000, 10, 4092),    # skinny nn
+    (1, 0, 1024, 10, 40000),   # skinny tn
+    (0, 1, 1000, 4096, 10),    # skinny nt (128-bit stores)
+    (0, 1, 100, 1030, 10),     # skinny nt (scalar stores)
+    (0, 0, 333, 1000, 777),    # CUDA-core tiles
+])
+@pytest.mark.parametrize("bias,acc,relu", [(False, False, False), (True, False, True), (True, True, False)])
+def test_masked_gemm_paths(ta, tb, M, N, K, bias, acc, relu):
+    out, ref, err = _masked(ta, tb, M, N, K, bias=bias, acc=acc, relu=relu)
+    assert err == 0
+    assert_close(out, ref, 1e-5, f"masked {ta}{tb} {M}x{N}x{K}")
+    # masked-out entries are exact zeros (or the accumulated value)
+    if not acc:
+        assert np.all(out[ref == 0] == 0)
+
+
+def test_folded_training_is_bit_identical():
+    tl = load_backend()
+    pr = tl.programs
+    ast = pr.mlp3_train(B=512, I=64, H=384, C=10, epochs=3)
+    feeds = pr.mlp3_inputs(B=512, I=64, H=384, C=10, seed=3)
+    fetch = ["loss", "W1", "b1", "W2", "b2", "W3", "b3"]
+    fused = tl.Program(ast, None, feeds=feeds, fetch=fetch)
+    a = fused.run()
+    names = [getattr(s, "fname", "") for s in fused._all_steps()]
+    fused.free()
+    assert names.count("tl_gemm_masked") == 2
+    b = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_ops=False).run()
+    for k in fetch:
+        assert np.array_equal(np.asarray(a[k]), np.asarray(b[k])), k
