@@ -339,10 +339,13 @@ def run_ours(args, rank, world, local):
 
 def run_micro(args):
     """One kernel alone, for profiling and per-kernel rooflines:
-    gemm     65536/8 x 4096 x 4096 linear forward (A 128 MiB, B 64 MiB)
-    fused    the [8192,8192] fused elementwise chain
-    softmax  softmax over rows of [16384,4096]
-    rowsum   sum over rows of [16384,4096]
+    gemm        65536/8 x 4096 x 4096 linear forward (A 128 MiB, B 64 MiB)
+    fused       the [8192,8192] fused elementwise chain
+    softmax     softmax over rows of [16384,4096]
+    rowsum      sum over rows of [16384,4096]
+    reductions  every reduction / normalisation of the [16384,4096] workload,
+                one JSON line each (the tensor is x ~ N(0,1); arg-reductions
+                read copies with 1% tied extremes per line)
     """
     from __graft_entry__ import load_package
     tl = load_package()
@@ -352,6 +355,26 @@ def run_micro(args):
     st = dev.stream
     hbm, bf16, _, src = peaks()
     reps = args.steps
+    if args.micro == "reductions":
+        pr = tl.programs
+        R, C_ = 16384, 4096
+        P = tl.Program(pr.reductions(R, C_), None, feeds=pr.reductions_inputs(R, C_),
+                       fetch=[n for n, _, _ in pr.REDUCTION_OPS] + ["sm", "ln"])
+        P.prepare()
+        for s in P._all_steps():
+            call = s.bind(P)
+            for _ in range(max(3, args.warmup)):
+                call()
+            P.sync()
+            ms = time_events(tl, st, call, reps)
+            two_way = s.label.split(":")[0] in ("softmax", "layer_norm_2d")
+            nbytes = 4.0 * R * C_ * (2 if two_way else 1)
+            ach = nbytes / (ms * 1e-3) / 1e9
+            print(json.dumps({"micro": "reductions", "op": s.label, "ms_per_launch": ms,
+                              "achieved": ach, "unit": "GB/s", "peak": hbm, "frac": ach / hbm,
+                              "peak_source": src, "launches": reps}), flush=True)
+        P.free()
+        return 0
     if args.micro == "gemm":
         M, N, K = 8192, 4096, 4096
         rng = np.random.default_rng(0)
@@ -402,7 +425,8 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fused", action="store_true")
-    ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum"], default=None,
+    ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum", "reductions"],
+                    default=None,
                     help="time one kernel alone (profiling aid); prints its own JSON line")
     args = ap.parse_args()
     if args.micro:

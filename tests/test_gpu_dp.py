@@ -3,8 +3,10 @@
 Runs ``tests/dp_worker.py`` under ``torch.distributed.run`` (one process per
 GPU, NCCL over NVLink), then the same program on one GPU, and compares the
 parameters after 4 epochs (rel 1e-4: the all-reduced gradient sums the
-shards in a different order than one GPU sums the whole batch).  Skipped
-when fewer than 2 GPUs are visible.
+shards in a different order than one GPU sums the whole batch).  The hidden
+biases start at +-0.5 so that no relu decision sits at float32 rounding
+distance from 0 (dp_worker.margin_biases).  Skipped when fewer than 2 GPUs
+are visible.
 """
 import ctypes
 import os
@@ -15,6 +17,7 @@ import numpy as np
 import pytest
 
 from conftest import REPO, assert_close, load_backend
+from dp_worker import margin_biases
 from oracle import OracleProgram
 
 pytestmark = pytest.mark.gpu
@@ -41,7 +44,7 @@ def test_dp2_matches_single_gpu(tmp_path):
     tl = load_backend()
     kw = dict(B=512, I=64, H=128, C=10)
     ast = tl.programs.mlp3_train(epochs=4, **kw)
-    feeds = tl.programs.mlp3_inputs(seed=5, **kw)
+    feeds = margin_biases(tl.programs.mlp3_inputs(seed=5, **kw))
     P = tl.Program(ast, None, feeds=feeds, fetch=list(got.files))
     single = P.run()
     P.free()
