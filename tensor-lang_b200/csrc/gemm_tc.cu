@@ -241,7 +241,26 @@ struct Params {
   int epilogue;
   const float* mask;  // relu-mask epilogue: C = v * (mask > 0), or null
   int64_t ldm;
+  int splits;         // CTA-pair kernel: K split this many ways (1: no split)
+  float* partial;     // [splits][M][N] raw sums when splits > 1
 };
+
+// Split-K partial of one thread's BN/2 columns of row `row` (no epilogue).
+__device__ __forceinline__ void store_partial(const Params& p, int split, int row, int nb0,
+                                              const float (&sum)[BN / 2]) {
+  if (row >= p.M || nb0 >= p.N) return;
+  float* prow = p.partial + ((int64_t)split * p.M + row) * p.N + nb0;
+  if (nb0 + BN / 2 <= p.N && (p.N % 4 == 0)) {
+    float4* p4 = reinterpret_cast<float4*>(prow);
+#pragma unroll
+    for (int j = 0; j < BN / 8; ++j)
+      __stcg(p4 + j, make_float4(sum[4 * j], sum[4 * j + 1], sum[4 * j + 2], sum[4 * j + 3]));
+  } else {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j)
+      if (nb0 + j < p.N) prow[j] = sum[j];
+  }
+}
 
 // Epilogue of one thread's BN/2 columns of row `row` (bias, relu, relu mask,
 // accumulate, store); shared by the single-CTA and CTA-pair kernels.
@@ -600,13 +619,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // clusters walk the N tiles first, so a wave's clusters share A row blocks in L2
-  const int n_tiles = (p.N + 255) / 256;
+  // clusters walk the N tiles first, so a wave's clusters share A row blocks in
+  // L2; with split K, all tiles of split 0 come first, then split 1, ...
+  const int n_tiles = (p.N + 255) / 256, m_tiles = (p.M + 255) / 256;
   const int cid = (int)(blockIdx.x >> 1);
-  const int m0 = (cid / n_tiles) * 256 + 128 * (int)rank;  // this CTA's rows of A and C
-  const int n0 = (cid % n_tiles) * 256;                    // the tile's columns
+  const int split = cid / (m_tiles * n_tiles), tile = cid % (m_tiles * n_tiles);
+  const int m0 = (tile / n_tiles) * 256 + 128 * (int)rank;  // this CTA's rows of A and C
+  const int n0 = (tile % n_tiles) * 256;                    // the tile's columns
   const int nb = n0 + HB * (int)rank;                              // this CTA's rows of B (N)
-  const int nk = (p.K + BK - 1) / BK;
+  const int nk_all = (p.K + BK - 1) / BK;
+  const int kb0 = (int)((int64_t)split * nk_all / p.splits);       // this split's k-blocks
+  const int nk = (int)((int64_t)(split + 1) * nk_all / p.splits) - kb0;
   const int nchunks = (nk + KC - 1) / KC;
 
   if (threadIdx.x == 0) {
@@ -646,7 +669,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         const uint32_t sB = sAx + A_TILE, sBx = sB + B_HALF;
         const uint32_t fb = full0 + 8u * (uint32_t)s;
         if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * STAGE2_BYTES);
-        const int k0 = kb * BK;
+        const int k0 = (kb0 + kb) * BK;
         if (TA == 0) {
           tma_load_2d_pair(sA, &tmA, fb, k0, m0);
           if (!PAIR) tma_load_2d_pair(sAx, &tmAx, fb, k0, m0);
@@ -771,7 +794,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
     }
-    if (ok) store_row(p, row, n0 + half * (BN / 2), sum);
+    if (ok) {
+      if (p.splits > 1)
+        store_partial(p, split, row, n0 + half * (BN / 2), sum);
+      else
+        store_row(p, row, n0 + half * (BN / 2), sum);
+    }
   }
   fence_before();
   cluster_sync_all();  // neither CTA releases TMEM or exits while the pair is still working
@@ -779,6 +807,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     fence_after();
     asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS)
                  : "memory");
+  }
+}
+
+// Split-K fold: C = epilogue(sum over splits of the partial sums, in split
+// order), four columns per thread when N is a multiple of 4.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(Params p) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const int64_t mn = (int64_t)p.M * p.N;
+  if (p.N % 4 == 0 && p.ldc % 4 == 0 && (((uintptr_t)p.C & 15) == 0)) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < mn / 4; i += stride) {
+      float4 v = __ldcs(reinterpret_cast<const float4*>(p.partial) + i);
+      for (int s = 1; s < p.splits; ++s) {
+        const float4 q = __ldcs(reinterpret_cast<const float4*>(p.partial + (int64_t)s * mn) + i);
+        v.x += q.x; v.y += q.y; v.z += q.z; v.w += q.w;
+      }
+      const int64_t e = 4 * i, row = e / p.N, col = e - row * p.N;
+      float o[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        if (p.bias) o[c] += p.bias[col + c];
+        if (p.epilogue == TL_EPI_RELU) o[c] = fmaxf(0.f, o[c]);
+        if (p.mask) o[c] = __fmul_rn(o[c], p.mask[row * p.ldm + col + c] > 0.f ? 1.f : 0.f);
+      }
+      float4* c4 = reinterpret_cast<float4*>(p.C + row * p.ldc + col);
+      if (p.accumulate) {
+        const float4 q = *c4;
+        o[0] = q.x + o[0]; o[1] = q.y + o[1]; o[2] = q.z + o[2]; o[3] = q.w + o[3];
+      }
+      *c4 = make_float4(o[0], o[1], o[2], o[3]);
+    }
+  } else {
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < mn; e += stride) {
+      float v = p.partial[e];
+      for (int s = 1; s < p.splits; ++s) v += p.partial[(int64_t)s * mn + e];
+      const int64_t row = e / p.N, col = e - row * p.N;
+      if (p.bias) v += p.bias[col];
+      if (p.epilogue == TL_EPI_RELU) v = fmaxf(0.f, v);
+      if (p.mask) v = __fmul_rn(v, p.mask[row * p.ldm + col] > 0.f ? 1.f : 0.f);
+      float* c = p.C + row * p.ldc + col;
+      *c = p.accumulate ? *c + v : v;
+    }
   }
 }
 
@@ -909,6 +978,7 @@ struct Workspace {
   size_t floats = 0;
 };
 Workspace g_ws[64];
+Workspace g_ws_partial[64];  // split-K partial sums
 std::vector<float*> g_retired;  // kept alive: captured graphs may still point at them
 
 bool load_encode() {
@@ -963,12 +1033,12 @@ bool make_pair_map_mn(CUtensorMap* m, const __nv_bfloat16* base, int64_t rp, int
 
 // Split workspace, grown on demand outside stream capture and never freed
 // (graphs captured earlier may still reference an older buffer).
-int workspace(size_t floats, float** out, cudaStream_t st) {
+int workspace(size_t floats, float** out, cudaStream_t st, Workspace* slots = g_ws) {
   int dev = 0;
   TL_CUDA_TRY(cudaGetDevice(&dev));
   if (dev < 0 || dev >= 64) return TL_ERR_INVALID_ARG;
   std::lock_guard<std::mutex> lk(g_ws_mu);
-  Workspace& w = g_ws[dev];
+  Workspace& w = slots[dev];
   if (w.floats < floats) {
     cudaStreamCaptureStatus cs;
     if (cudaStreamIsCapturing(st, &cs) == cudaSuccess && cs != cudaStreamCaptureStatusNone)
@@ -988,6 +1058,23 @@ int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both 
 int g_scheme = kSchemeTF32BF16;
 int g_cta_pair = 1;  // 256 x 256 CTA-pair tiles when the product has more than one row tile
 
+// K splits for the CTA-pair kernel: a product of only a few waves of cluster
+// tiles leaves most SM pairs idle in its last wave (e.g. 256 tiles on 74
+// pairs: 3.46 waves, 86% busy).  Split K so that tiles x splits fill whole
+// waves (>= 95%), keeping at least 8 k-blocks (256 of K) per split.
+int split_count(int64_t clusters, int64_t nk) {
+  const int64_t slots = sm_count() / 2;
+  if (slots < 1 || clusters >= 8 * slots) return 1;
+  auto eff = [&](int64_t s) {
+    const int64_t work = clusters * s, waves = (work + slots - 1) / slots;
+    return (double)work / (double)(waves * slots);
+  };
+  if (eff(1) >= 0.95) return 1;
+  for (int s = 2; s <= 8; ++s)
+    if (nk / s >= 8 && eff(s) >= 0.95) return s;
+  return 1;
+}
+
 // Launch the single-CTA or the CTA-pair kernel over prepared tensor maps.
 template <int TA, int TB, int SCHEME>
 int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CUtensorMap& mb,
@@ -996,8 +1083,23 @@ int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CU
     auto kern = gemm_tc2_kernel<TA, TB, SCHEME>;
     TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES));
     const int64_t clusters = ((M + 255) / 256) * ((N + 255) / 256);
-    if (2 * clusters > INT32_MAX) return TL_ERR_UNSUPPORTED;
-    kern<<<(unsigned)(2 * clusters), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, p);
+    const int splits = split_count(clusters, (p.K + BK - 1) / BK);
+    if (2 * clusters * splits > INT32_MAX) return TL_ERR_UNSUPPORTED;
+    Params q = p;
+    q.splits = splits;
+    if (splits > 1) {
+      float* part = nullptr;
+      TL_TRY(workspace((size_t)splits * M * N, &part, st, g_ws_partial));
+      q.partial = part;
+    }
+    kern<<<(unsigned)(2 * clusters * splits), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, q);
+    if (splits > 1) {
+      TL_TRY(after_launch());
+      const int64_t units = (N % 4 == 0) ? M * N / 4 : M * N;
+      const int64_t cap = 8LL * sm_count();
+      splitk_reduce_kernel<<<(unsigned)((units + 255) / 256 < cap ? (units + 255) / 256 : cap), 256, 0,
+                             st>>>(q);
+    }
   } else {
     auto kern = gemm_tc_kernel<TA, TB, SCHEME>;
     TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
@@ -1052,7 +1154,7 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
       !(TA ? make_pair_map_mn(&map_, ap, mp, kp) : make_pair_map(&map_, ap, M, kp, BM)) ||
       !(TB ? make_pair_map(&mbp, bp, N, kp, b_box) : make_pair_map_mn(&mbp, bp, np_, kp)))
     return TL_ERR_UNSUPPORTED;
-  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm};
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm, 1, nullptr};
   return run_tiles<TA, TB, kSchemeTF32BF16>(two, ma, map_, mb, mbp, p, M, N, st);
 }
 
@@ -1105,7 +1207,7 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
       !make_map(&mb, b_hi, b_rows, b_cols, ldb, b_inner, b_outer, b_mn) ||
       !make_map(&mbl, b_lo, b_rows, b_cols, ldb, b_inner, b_outer, b_mn))
     return TL_ERR_UNSUPPORTED;
-  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm};
+  Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm, 1, nullptr};
   return run_tiles<TA, TB, kScheme3xTF32>(two, ma, mal, mb, mbl, p, M, N, st);
 }
 

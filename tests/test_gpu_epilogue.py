@@ -86,3 +86,15 @@ def test_folded_training_is_bit_identical():
     b = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_ops=False).run()
     for k in fetch:
         assert np.array_equal(np.asarray(a[k]), np.asarray(b[k])), k
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(1024, 4096, 2048),   # 64 cluster tiles: K split 8 ways
+                                   (4096, 4096, 512)])   # 256 cluster tiles: K split 2 ways
+@pytest.mark.parametrize("bias,acc,relu", [(True, False, True), (False, True, False)])
+def test_split_k_gemm(ta, tb, M, N, K, bias, acc, relu):
+    """Products of a few waves of 256 x 256 tiles split K across CTA pairs and
+    fold the partial sums in split order before the epilogue."""
+    out, ref, err = _masked(ta, tb, M, N, K, bias=bias, acc=acc, relu=relu)
+    assert err == 0
+    assert_close(out, ref, 1e-5, f"split-K {ta}{tb} {M}x{N}x{K}")
