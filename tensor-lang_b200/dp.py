@@ -3,9 +3,12 @@
 The reference has no multi-GPU path (README.md:583 lists it as future work).
 This module runs one process per GPU: the batch axis of the designated input
 tensors is split contiguously (rank r holds rows [r*B/P, (r+1)*B/P)), every
-rank holds full parameter replicas, and after each backward the gradients of
-the replicated tensors are summed across ranks with one NCCL all-reduce over
-NVLink (libtlb200 ``tl_nccl_allreduce_sum``).  The cross_entropy and mse_loss
+rank holds full parameter replicas, and the gradients of the replicated
+tensors are summed across ranks by NCCL all-reduces over NVLink (libtlb200
+``tl_nccl_allreduce_sum``) on a communication stream: gradients are grouped
+into buckets in the order backward finalises them, and each bucket's
+all-reduce starts as soon as its last gradient is written, overlapping the
+rest of backward; the update waits for all of them.  The cross_entropy and mse_loss
 VJPs divide by the *global* batch (autograd.py:686,700), so the summed
 gradients equal the single-GPU ones and the replicated SGD update keeps the
 replicas identical.
@@ -21,7 +24,7 @@ import pickle
 import socket
 import struct
 import time
-from typing import Dict, Iterable, List, Optional, Sequence
+from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
 import numpy as np
 
@@ -134,6 +137,7 @@ class Communicator:
         self.world, self.rank = rdv.world, rdv.rank
         self.timeout_ms = timeout_ms
         self.handle = None
+        self.stream = None  # communication stream of this rank's device
         if self.world == 1:
             return
         # NVLink SHARP (NVLS) stays off unless the caller enables it: it binds
@@ -151,17 +155,23 @@ class Communicator:
         rt.check(L.tl_nccl_comm_init(ctypes.byref(h), self.world, uid, self.rank, timeout_ms),
                  "nccl_comm_init")
         self.handle = h.value
+        s = ctypes.c_void_p()
+        rt.check(L.tl_stream_create(ctypes.byref(s)), "stream_create")
+        self.stream = s.value
 
     def wait(self, stream, timeout_ms: Optional[int] = None):
         if self.handle:
-            rt.check(rt.lib().tl_nccl_wait(self.handle, stream,
-                                           self.timeout_ms if timeout_ms is None else timeout_ms),
-                     "nccl_wait")
+            t = self.timeout_ms if timeout_ms is None else timeout_ms
+            for st in (stream, self.stream):
+                rt.check(rt.lib().tl_nccl_wait(self.handle, st, t), "nccl_wait")
 
     def destroy(self):
         if self.handle:
             rt.lib().tl_nccl_comm_destroy(self.handle)
             self.handle = None
+        if self.stream:
+            rt.lib().tl_stream_destroy(self.stream)
+            self.stream = None
 
     def abort(self):
         if self.handle:
@@ -169,34 +179,101 @@ class Communicator:
             self.handle = None
 
 
-class AllReduce(Step):
-    """Sum the named gradients across ranks (one NCCL call per contiguous run)."""
+class AllReduceBucket(Step):
+    """Sum one bucket of gradients across ranks, on the communication stream.
 
-    def __init__(self, names: Sequence[str], comm: Communicator):
+    The bucket's gradients are consecutive in the arena, so one NCCL call
+    covers them (padding between them is summed too, harmlessly).  The
+    communication stream first waits for everything the main stream issued
+    so far -- the steps that wrote these gradients."""
+
+    def __init__(self, names: Sequence[str], comm: Communicator, index: int):
         self.names = list(names)
         self.comm = comm
         self.reads, self.writes = list(names), list(names)
-        self.label = "allreduce:" + ",".join(names)
+        self.label = f"allreduce{index}:" + ",".join(names)
+        self._event = None
 
     def bind(self, P):
         L = rt.lib()
-        spans = []
-        arena = P.arena_span()
-        if arena is not None and set(self.names) <= set(P.arena_names):
-            spans.append(list(arena))  # one call over the packed arena
-        else:
-            for n in self.names:
-                p, cnt = P.ptr(n), numel(P.shapes[n])
-                if spans and spans[-1][0] + 4 * spans[-1][1] == p:
-                    spans[-1][1] += cnt
-                else:
-                    spans.append([p, cnt])
-        h, stream = self.comm.handle, P.stream
+        first, last = self.names[0], self.names[-1]
+        p0 = P.ptr(first)
+        count = (P.ptr(last) - p0) // 4 + numel(P.shapes[last])
+        ev = ctypes.c_void_p()
+        rt.check(L.tl_event_create(ctypes.byref(ev)), "event_create")
+        self._event = ev.value
+        h, main, comm_st, label = self.comm.handle, P.stream, self.comm.stream, self.label
 
         def run():
-            for p, cnt in spans:
-                rt.check(L.tl_nccl_allreduce_sum(h, p, cnt, stream), "nccl_allreduce")
+            rt.check(L.tl_event_record(self._event, main), label)
+            rt.check(L.tl_stream_wait_event(comm_st, self._event), label)
+            rt.check(L.tl_nccl_allreduce_sum(h, p0, count, comm_st), label)
         return run
+
+
+class AllReduceJoin(Step):
+    """The main stream waits for every bucket's all-reduce."""
+
+    def __init__(self, names: Sequence[str], comm: Communicator):
+        self.comm = comm
+        self.reads, self.writes = list(names), list(names)
+        self.label = "allreduce_join"
+
+    def bind(self, P):
+        L = rt.lib()
+        ev = ctypes.c_void_p()
+        rt.check(L.tl_event_create(ctypes.byref(ev)), "event_create")
+        e, main, comm_st = ev.value, P.stream, self.comm.stream
+
+        def run():
+            rt.check(L.tl_event_record(e, comm_st), self.label)
+            rt.check(L.tl_stream_wait_event(main, e), self.label)
+        return run
+
+
+BUCKET_BYTES = 16 << 20  # a bucket closes once it holds this much
+
+
+def plan_buckets(bw: List[Step], grads: Sequence[str], shapes: Dict[str, Shape],
+                 comm: Communicator) -> Tuple[List[Step], List[str]]:
+    """Insert bucketed all-reduces into the backward steps ``bw``.
+
+    A gradient is final after the last backward step that reads or writes it;
+    gradients are taken in the order they become final, and a bucket closes
+    (its all-reduce is inserted right after that step) once it holds
+    ``BUCKET_BYTES``; what is left joins the last bucket, issued at the end.
+    Returns the new step list and the arena order (buckets contiguous)."""
+    last = {}
+    for i, st in enumerate(bw):
+        for n in set(st.reads) | set(st.writes):
+            if n in grads:
+                last[n] = i
+    order = sorted(grads, key=lambda n: (last.get(n, -1), grads.index(n)))
+    buckets, cur, size = [], [], 0
+    for n in order:
+        cur.append(n)
+        size += 4 * numel(shapes[n])
+        if size >= BUCKET_BYTES:
+            buckets.append(cur)
+            cur, size = [], 0
+    if cur:
+        if buckets:
+            buckets[-1] = buckets[-1] + cur  # the tail goes out with the last bucket
+        else:
+            buckets.append(cur)
+    after = {}
+    for bi, names in enumerate(buckets):
+        pos = max(last.get(n, -1) for n in names)
+        pos = len(bw) - 1 if bi == len(buckets) - 1 else pos
+        after.setdefault(pos, []).append(AllReduceBucket(names, comm, bi))
+    out: List[Step] = []
+    for step in after.get(-1, []):
+        out.append(step)
+    for i, st in enumerate(bw):
+        out.append(st)
+        out.extend(after.get(i, []))
+    out.append(AllReduceJoin(list(grads), comm))
+    return out, [n for names in buckets for n in names]
 
 
 # ---------------------------------------------------------------------------
@@ -277,11 +354,15 @@ class DataParallelProgram:
         self.global_shapes = gshapes
         self.replicated_grads: List[str] = []
 
-        def hook(prog, exposed):
+        def hook(prog, exposed, bw):
             names = [f"{n}_grad" for n in exposed if n not in self.derived]
             self.replicated_grads = names
             prog.arena_names = list(names)
-            return [AllReduce(names, comm)] if comm.world > 1 and names else []
+            if comm.world == 1 or not names:
+                return bw
+            bw, arena_order = plan_buckets(bw, names, prog.shapes, comm)
+            prog.arena_names = arena_order
+            return bw
 
         self.program = Program(ast, None, device=device, feeds=feeds, fetch=fetch, shapes=local,
                                divisors=divisors, grad_hook=hook, use_graphs=use_graphs)

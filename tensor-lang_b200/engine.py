@@ -215,7 +215,7 @@ class Program:
         self.fuse_ops = fuse_ops
         self.save_dir = Path(save_dir) if save_dir else Path.cwd()
         self.divisors = divisors or {}
-        self.grad_hook = grad_hook  # called with (exposed grads) -> extra steps (data parallel)
+        self.grad_hook = grad_hook  # (program, exposed grads, backward steps) -> backward steps
         self.arena_names: List[str] = []  # allocated contiguously (one all-reduce span)
         self.gen = KernelGenerator(False)
         self.nodes: List[Node] = []
@@ -355,7 +355,7 @@ class Program:
             bw_steps, exposed = planner.plan(body[bw]["loss_tensor"])
             self.exposed_grads = sorted(set(self.exposed_grads) | set(exposed))
             if self.grad_hook is not None:
-                bw_steps = bw_steps + self.grad_hook(self, exposed)
+                bw_steps = self.grad_hook(self, exposed, bw_steps)
         rebinds = [b for b in body if b["type"] == "rebind" and b["expr"].get("type") == "name"]
         reb_steps = self._plan_rebinds(rebinds, pre + bw_steps + post)
         return _Loop(int(node["iterations"]), pre, bw_steps, post, reb_steps, label)
