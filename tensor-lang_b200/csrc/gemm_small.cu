@@ -274,7 +274,9 @@ __global__ void __launch_bounds__(256, 2) small_nn4_kernel(int64_t M, int N, int
 // block): a persistent grid of one 512-thread block per SM walks 64-row
 // groups (12 warps x RPW rows), so B is read from global memory once per SM
 // instead of once per row group.  Needs NB*(K+4)*4 bytes of shared memory.
-// 12 warps: up to 170 registers a thread, 8 loads of 16 bytes in flight each.
+// 12 warps: up to 170 registers a thread, 12 loads of 16 bytes in flight each.
+// (Per float4 of A the kernel issues NB/4 shared loads and 4*NB FMAs per row;
+// with N = 10 that is about half of HBM speed at 4 instructions a clock.)
 constexpr int kNnpWarps = 12;
 template <int NB, int RPW>
 __global__ void __launch_bounds__(32 * kNnpWarps, 1) small_nn4p_kernel(int64_t M, int N, int64_t K,
@@ -320,8 +322,8 @@ __global__ void __launch_bounds__(32 * kNnpWarps, 1) small_nn4p_kernel(int64_t M
     for (int r = 0; r < RPW; ++r)
 #pragma unroll
       for (int n = 0; n < NB; ++n) acc[r][n] = 0.f;
-#pragma unroll 2
-    for (int q = lane; q < nq; q += 32) {
+#pragma unroll 3
+    for (int q = lane; q < nq; q += 32) {  // 3 trips unrolled: 12 loads of 16 B in flight a lane
       float4 a[RPW];
 #pragma unroll
       for (int r = 0; r < RPW; ++r) a[r] = ld_stream4(arow[r] + 4 * q);
@@ -408,7 +410,7 @@ __global__ void __launch_bounds__(256, 2) small_tn4_kernel(int64_t M, int N, int
     }
     __syncthreads();
     if (mv) {
-#pragma unroll 4
+#pragma unroll 8
       for (int kk = warp; kk < kt; kk += 8) {
         const float4 a = ld_stream4(A + (k0 + kk) * lda + m);
 #pragma unroll
@@ -509,6 +511,7 @@ __global__ void __launch_bounds__(256) small_nt4_kernel(int64_t M, int64_t N, in
   }
   __syncthreads();
   if (n >= N) return;
+  const bool mask4 = mask && (ldm % 4 == 0) && ((((uintptr_t)mask) & 15) == 0);
   for (int r = 0; r < mr; ++r) {
     float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
@@ -526,7 +529,16 @@ __global__ void __launch_bounds__(256) small_nt4_kernel(int64_t M, int64_t N, in
     for (int c = 0; c < 4; ++c) {
       v[c] += bn[c];
       if (relu) v[c] = fmaxf(0.f, v[c]);
-      v[c] = mask_of(v[c], mask, ldm, m0 + r, n + c);
+    }
+    if (mask4) {
+      const float4 mk = __ldg(reinterpret_cast<const float4*>(mask + (m0 + r) * ldm + n));
+      v[0] = __fmul_rn(v[0], mk.x > 0.f ? 1.f : 0.f);
+      v[1] = __fmul_rn(v[1], mk.y > 0.f ? 1.f : 0.f);
+      v[2] = __fmul_rn(v[2], mk.z > 0.f ? 1.f : 0.f);
+      v[3] = __fmul_rn(v[3], mk.w > 0.f ? 1.f : 0.f);
+    } else {
+#pragma unroll
+      for (int c = 0; c < 4; ++c) v[c] = mask_of(v[c], mask, ldm, m0 + r, n + c);
     }
     float4* c4 = reinterpret_cast<float4*>(C + (m0 + r) * ldc + n);
     float4 o = make_float4(v[0], v[1], v[2], v[3]);
@@ -587,16 +599,17 @@ struct RunNN {
   static int run(int64_t M, int N, int64_t K, const float* A, int64_t lda, const float* B,
                  int64_t ldb, float* C, int64_t ldc, const float* bias, int acc, int relu, const float* mask, int64_t ldm,
                  cudaStream_t st) {
-    constexpr int RPW = NB <= 12 ? 4 : 2;
+    constexpr int RPW = NB <= 12 ? 4 : 2;   // nn4 / nn kernels (8 warps a block)
+    constexpr int RPWP = RPW;               // persistent nn4p (12 warps a block)
     const int64_t blocks = (M + 8 * RPW - 1) / (8 * RPW);
     if (blocks > INT32_MAX) return TL_ERR_UNSUPPORTED;
     if (K % 4 == 0 && lda % 4 == 0 && aligned16(A)) {
       if constexpr (NB <= 16) {
         const size_t smem = (size_t)NB * (K + 4) * 4;
         if (smem <= 200 * 1024) {
-          auto kern = small_nn4p_kernel<NB, RPW>;
+          auto kern = small_nn4p_kernel<NB, RPWP>;
           TL_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-          const int64_t groups = (M + kNnpWarps * RPW - 1) / (kNnpWarps * RPW);
+          const int64_t groups = (M + kNnpWarps * RPWP - 1) / (kNnpWarps * RPWP);
           const unsigned grid = (unsigned)(groups < sm_count() ? groups : sm_count());
           kern<<<grid, 32 * kNnpWarps, smem, st>>>(M, N, K, A, lda, B, ldb, C, ldc, bias, acc, relu, mask, ldm);
           return after_launch();
