@@ -512,41 +512,77 @@ __global__ void __launch_bounds__(256) small_nt4_kernel(int64_t M, int64_t N, in
   __syncthreads();
   if (n >= N) return;
   const bool mask4 = mask && (ldm % 4 == 0) && ((((uintptr_t)mask) & 15) == 0);
-  for (int r = 0; r < mr; ++r) {
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
+  if (!mask4) {  // no mask operand: one row at a time keeps the registers (occupancy) low
+    for (int r = 0; r < mr; ++r) {
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int q = 0; q < KB / 4; ++q) {
-      const float4 a = *reinterpret_cast<const float4*>(&As4[r * KB + 4 * q]);
+      for (int q = 0; q < KB / 4; ++q) {
+        const float4 a = *reinterpret_cast<const float4*>(&As4[r * KB + 4 * q]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          v[c] = fmaf(a.x, b[c][4 * q], v[c]);
+          v[c] = fmaf(a.y, b[c][4 * q + 1], v[c]);
+          v[c] = fmaf(a.z, b[c][4 * q + 2], v[c]);
+          v[c] = fmaf(a.w, b[c][4 * q + 3], v[c]);
+        }
+      }
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        v[c] = fmaf(a.x, b[c][4 * q], v[c]);
-        v[c] = fmaf(a.y, b[c][4 * q + 1], v[c]);
-        v[c] = fmaf(a.z, b[c][4 * q + 2], v[c]);
-        v[c] = fmaf(a.w, b[c][4 * q + 3], v[c]);
+        v[c] += bn[c];
+        if (relu) v[c] = fmaxf(0.f, v[c]);
+        if (mask) v[c] = mask_of(v[c], mask, ldm, m0 + r, n + c);
       }
+      float4* c4 = reinterpret_cast<float4*>(C + (m0 + r) * ldc + n);
+      float4 o = make_float4(v[0], v[1], v[2], v[3]);
+      if (accumulate) {
+        const float4 q = *c4;
+        o.x = q.x + o.x; o.y = q.y + o.y; o.z = q.z + o.z; o.w = q.w + o.w;
+      }
+      *c4 = o;
     }
+    return;
+  }
+  // with a mask: rows in groups of 4, the group's mask vectors loaded before
+  // any of its rows is computed, so 4 loads of 16 bytes are in flight a thread
+  for (int r0 = 0; r0 < mr; r0 += 4) {
+    float4 mk[4];
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      v[c] += bn[c];
-      if (relu) v[c] = fmaxf(0.f, v[c]);
-    }
-    if (mask4) {
-      const float4 mk = __ldg(reinterpret_cast<const float4*>(mask + (m0 + r) * ldm + n));
-      v[0] = __fmul_rn(v[0], mk.x > 0.f ? 1.f : 0.f);
-      v[1] = __fmul_rn(v[1], mk.y > 0.f ? 1.f : 0.f);
-      v[2] = __fmul_rn(v[2], mk.z > 0.f ? 1.f : 0.f);
-      v[3] = __fmul_rn(v[3], mk.w > 0.f ? 1.f : 0.f);
-    } else {
+    for (int i = 0; i < 4; ++i)
+      mk[i] = (r0 + i < mr) ? __ldg(reinterpret_cast<const float4*>(mask + (m0 + r0 + i) * ldm + n))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) v[c] = mask_of(v[c], mask, ldm, m0 + r, n + c);
+    for (int i = 0; i < 4; ++i) {
+      const int r = r0 + i;
+      if (r >= mr) break;
+      float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q = 0; q < KB / 4; ++q) {
+        const float4 a = *reinterpret_cast<const float4*>(&As4[r * KB + 4 * q]);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          v[c] = fmaf(a.x, b[c][4 * q], v[c]);
+          v[c] = fmaf(a.y, b[c][4 * q + 1], v[c]);
+          v[c] = fmaf(a.z, b[c][4 * q + 2], v[c]);
+          v[c] = fmaf(a.w, b[c][4 * q + 3], v[c]);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        v[c] += bn[c];
+        if (relu) v[c] = fmaxf(0.f, v[c]);
+      }
+      v[0] = __fmul_rn(v[0], mk[i].x > 0.f ? 1.f : 0.f);
+      v[1] = __fmul_rn(v[1], mk[i].y > 0.f ? 1.f : 0.f);
+      v[2] = __fmul_rn(v[2], mk[i].z > 0.f ? 1.f : 0.f);
+      v[3] = __fmul_rn(v[3], mk[i].w > 0.f ? 1.f : 0.f);
+      float4* c4 = reinterpret_cast<float4*>(C + (m0 + r) * ldc + n);
+      float4 o = make_float4(v[0], v[1], v[2], v[3]);
+      if (accumulate) {
+        const float4 q = *c4;
+        o.x = q.x + o.x; o.y = q.y + o.y; o.z = q.z + o.z; o.w = q.w + o.w;
+      }
+      *c4 = o;
     }
-    float4* c4 = reinterpret_cast<float4*>(C + (m0 + r) * ldc + n);
-    float4 o = make_float4(v[0], v[1], v[2], v[3]);
-    if (accumulate) {
-      const float4 q = *c4;
-      o.x = q.x + o.x; o.y = q.y + o.y; o.z = q.z + o.z; o.w = q.w + o.w;
-    }
-    *c4 = o;
   }
 }
 
