@@ -228,6 +228,39 @@ int  tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                     const float* A, int64_t lda, const float* B, int64_t ldb,
                     float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
                     const float* mask, int64_t ldm, void* stream);
+/* Precomputed bf16 pair matrices for the TF32+bf16 scheme (no reference
+ * counterpart).  The scheme multiplies hi*hi on TF32 and the corrections on
+ * a pair matrix per operand; tl_gemm computes those pairs itself on every
+ * call.  A caller that uses one operand in several products, or the same
+ * operand over many calls, prepares its pairs once:
+ *   tl_gemm_pair_bytes(rows, cols, layout)   bytes of the pair of X[rows][cols]
+ *     layout TL_PAIR_KMAJOR  (X is [MN][K]): rows x ceil32(cols) x 4
+ *     layout TL_PAIR_MNMAJOR (X is [K][MN]): ceil32(rows) x ceil8(cols) x 4
+ *   tl_gemm_pair_prepare(X, ld, rows, cols, kmajor, klo, mnmajor, mlo, stream)
+ *     writes either or both layouts from one read of X (16-byte aligned
+ *     outputs; null skips one); *lo_first = 1 for a B operand, 0 for A
+ *   tl_gemm_pairs(..., A, lda, a_pair, B, ldb, b_pair, ...)
+ *     tl_gemm_masked taking those pairs (null: computed inside as usual).
+ *     The layout an operand needs: A as stored (trans_a 0) -> K-major, A^T
+ *     (trans_a 1) -> MN-major; B^T as stored (trans_b 1) -> K-major, B
+ *     (trans_b 0) -> MN-major.  Paths other than the TF32+bf16 tensor-core
+ *     path ignore the pairs.
+ *   tl_gemm_uses_pairs(ta, tb, M, N, K, lda, ldb)  1 if such a call takes
+ *     that path (so prepared pairs are used), else 0; depends only on the
+ *     shapes and the selected scheme. */
+#define TL_PAIR_KMAJOR 0
+#define TL_PAIR_MNMAJOR 1
+int64_t tl_gemm_pair_bytes(int64_t rows, int64_t cols, int layout);
+int  tl_gemm_pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols,
+                          void* kmajor, int kmajor_lo_first, void* mnmajor,
+                          int mnmajor_lo_first, void* stream);
+int  tl_gemm_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+                   const float* A, int64_t lda, const void* a_pair,
+                   const float* B, int64_t ldb, const void* b_pair,
+                   float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
+                   const float* mask, int64_t ldm, void* stream);
+int  tl_gemm_uses_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
+                        int64_t lda, int64_t ldb);
 /* Which path tl_gemm would take (0 tensor-core, 1 CUDA-core) for this call. */
 int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                   const float* A, int64_t lda, const float* B, int64_t ldb,

@@ -16,7 +16,12 @@ namespace tl {
 
 int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
             const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
-            int epilogue, const float* mask, int64_t ldm, cudaStream_t st);
+            int epilogue, const float* mask, int64_t ldm, const void* a_pair, const void* b_pair,
+            cudaStream_t st);
+bool gemm_uses_pairs(int ta, int tb, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb);
+int64_t pair_bytes(int64_t rows, int64_t cols, int layout);
+int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                 int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st);
 bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                 const float* B, int64_t ldb, const float* C, int64_t ldc);
 void gemm_set_split_mode(int mode);
@@ -158,17 +163,17 @@ int gemm_simt(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, i
 
 extern "C" {
 
-int tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A,
-                   int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
-                   const float* bias, int accumulate, int epilogue, const float* mask,
-                   int64_t ldm, void* stream) {
+int tl_gemm_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A,
+                  int64_t lda, const void* a_pair, const float* B, int64_t ldb, const void* b_pair,
+                  float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
+                  const float* mask, int64_t ldm, void* stream) {
   if (M <= 0 || N <= 0 || !C) return TL_ERR_INVALID_ARG;
   if (K > 0 && (!A || !B)) return TL_ERR_INVALID_ARG;
   if (mask && ldm < N) return TL_ERR_INVALID_ARG;
   cudaStream_t st = tl::stream_or_default(stream);
   if (!tl::g_force_simt && tl::gemm_tc_ok(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc))
     return tl::gemm_tc(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
-                       epilogue, mask, ldm, st);
+                       epilogue, mask, ldm, a_pair, b_pair, st);
   if (K > 0 && tl::gemm_small_ok(trans_a, trans_b, M, N, K)) {
     int s = tl::gemm_small(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
                            epilogue, mask, ldm, st);
@@ -176,6 +181,31 @@ int tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, co
   }
   return tl::gemm_simt(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate,
                        epilogue, mask, ldm, st);
+}
+
+int tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A,
+                   int64_t lda, const float* B, int64_t ldb, float* C, int64_t ldc,
+                   const float* bias, int accumulate, int epilogue, const float* mask,
+                   int64_t ldm, void* stream) {
+  return tl_gemm_pairs(trans_a, trans_b, M, N, K, A, lda, nullptr, B, ldb, nullptr, C, ldc, bias,
+                       accumulate, epilogue, mask, ldm, stream);
+}
+
+int tl_gemm_uses_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, int64_t lda,
+                       int64_t ldb) {
+  return (!tl::g_force_simt && tl::gemm_uses_pairs(trans_a, trans_b, M, N, K, lda, ldb)) ? 1 : 0;
+}
+
+int64_t tl_gemm_pair_bytes(int64_t rows, int64_t cols, int layout) {
+  return tl::pair_bytes(rows, cols, layout);
+}
+
+int tl_gemm_pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                         int kmajor_lo_first, void* mnmajor, int mnmajor_lo_first, void* stream) {
+  if (!X || rows <= 0 || cols <= 0 || ld < cols || (!kmajor && !mnmajor)) return TL_ERR_INVALID_ARG;
+  if ((((uintptr_t)kmajor) & 15) || (((uintptr_t)mnmajor) & 15)) return TL_ERR_INVALID_ARG;
+  return tl::pair_prepare(X, ld, rows, cols, kmajor, kmajor_lo_first, mnmajor, mnmajor_lo_first,
+                          tl::stream_or_default(stream));
 }
 
 int tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,

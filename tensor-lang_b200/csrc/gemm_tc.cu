@@ -965,6 +965,52 @@ __global__ void __launch_bounds__(256) pair_mn_kernel(const float* __restrict__ 
   }
 }
 
+// Both pair layouts of X [R][C] (row stride ld) from one read: the K-major
+// pair (X as [rows = MN][cols = K]: P[r][64j + i], k = c = 32j + i) and the
+// MN-major pair (X as [rows = K][cols = MN]: rows 64j + i / 64j + 32 + i for
+// k = r = 32j + i, columns c < rp = ceil8(C)).  Either output may be null;
+// lo_first selects the B-operand ordering.  Padding (c >= C up to ceil32(C),
+// r >= R up to ceil32(R)) is written as zeros.
+__global__ void __launch_bounds__(256) pair_both_kernel(const float* __restrict__ X, int64_t ld,
+                                                        int64_t R, int64_t C,
+                                                        __nv_bfloat16* __restrict__ pk, int k_lo_first,
+                                                        __nv_bfloat16* __restrict__ pm, int m_lo_first) {
+  const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
+  const int64_t kpc = (C + 31) / 32 * 32;         // K-major row: 2 * kpc bf16
+  const int64_t rp = (C + 7) / 8 * 8;             // MN-major row length
+  const int64_t r_end = pm ? (R + 31) / 32 * 32 : R;
+  const int64_t c_end = pk ? kpc : rp;
+  for (int64_t r = blockIdx.x; r < r_end; r += gridDim.x) {
+    const float* src = X + r * ld;
+    __nv_bfloat16* kv = pk ? pk + r * 2 * kpc : nullptr;
+    __nv_bfloat16* mv = pm ? pm + (64 * (r >> 5) + (r & 31)) * rp : nullptr;
+    for (int64_t c = 8 * (int64_t)threadIdx.x; c < c_end; c += 8 * (int64_t)blockDim.x) {
+      float x[8];
+      if (r < R && vec && c + 7 < C) {
+        const float4 a = ld_stream4(src + c), b = ld_stream4(src + c + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = (r < R && c + i < C) ? src[c + i] : 0.f;
+      }
+      const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
+                                  pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])),
+                                  pack_bf16(lo_of(x[4]), lo_of(x[5])), pack_bf16(lo_of(x[6]), lo_of(x[7])));
+      if (kv && r < R) {
+        __nv_bfloat16* o = kv + 64 * (c >> 5) + (c & 31);
+        *reinterpret_cast<uint4*>(o) = k_lo_first ? lv : hv;
+        *reinterpret_cast<uint4*>(o + 32) = k_lo_first ? hv : lv;
+      }
+      if (mv && c < rp) {
+        *reinterpret_cast<uint4*>(mv + c) = m_lo_first ? lv : hv;
+        *reinterpret_cast<uint4*>(mv + 32 * rp + c) = m_lo_first ? hv : lv;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------- host side ---
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -1123,26 +1169,36 @@ unsigned pair_grid(int64_t units) {
 template <int TA, int TB>
 int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B,
                 int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
-                const float* mask, int64_t ldm, cudaStream_t st) {
+                const float* mask, int64_t ldm, const void* a_pre, const void* b_pre,
+                cudaStream_t st) {
   const int64_t kp = (K + 31) / 32 * 32;
   const int64_t mp = (M + 7) / 8 * 8, np_ = (N + 7) / 8 * 8;  // MN-major pair row lengths
-  // K-major pairs: [M][2kp]; MN-major pairs: [2kp][mp] (bf16, 4 bytes per element pair)
-  const size_t a_bytes = ((size_t)(TA ? mp : M) * kp * 4 + 1023) / 1024 * 1024;
-  const size_t b_bytes = ((size_t)(TB ? N : np_) * kp * 4 + 1023) / 1024 * 1024;
+  // K-major pairs: [M][2kp]; MN-major pairs: [2kp][mp] (bf16, 4 bytes per element pair);
+  // a pair the caller computed already (a_pre / b_pre) is used as it is
+  const size_t a_bytes = a_pre ? 0 : ((size_t)(TA ? mp : M) * kp * 4 + 1023) / 1024 * 1024;
+  const size_t b_bytes = b_pre ? 0 : ((size_t)(TB ? N : np_) * kp * 4 + 1023) / 1024 * 1024;
   float* ws = nullptr;
-  TL_TRY(workspace((a_bytes + b_bytes) / 4, &ws, st));
-  __nv_bfloat16* ap = reinterpret_cast<__nv_bfloat16*>(ws);
-  __nv_bfloat16* bp = reinterpret_cast<__nv_bfloat16*>((char*)ws + a_bytes);
-  if (TA == 0)
-    pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, ap);
-  else
-    pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(A, lda, K, M, mp, kp, 0, ap);
-  TL_TRY(after_launch());
-  if (TB == 1)
-    pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, bp);
-  else
-    pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(B, ldb, K, N, np_, kp, 1, bp);
-  TL_TRY(after_launch());
+  if (a_bytes + b_bytes) TL_TRY(workspace((a_bytes + b_bytes) / 4, &ws, st));
+  const __nv_bfloat16* ap = reinterpret_cast<const __nv_bfloat16*>(a_pre);
+  const __nv_bfloat16* bp = reinterpret_cast<const __nv_bfloat16*>(b_pre);
+  if (!a_pre) {
+    __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>(ws);
+    if (TA == 0)
+      pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, w);
+    else
+      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(A, lda, K, M, mp, kp, 0, w);
+    TL_TRY(after_launch());
+    ap = w;
+  }
+  if (!b_pre) {
+    __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>((char*)ws + a_bytes);
+    if (TB == 1)
+      pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, w);
+    else
+      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(B, ldb, K, N, np_, kp, 1, w);
+    TL_TRY(after_launch());
+    bp = w;
+  }
 
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
   const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
@@ -1161,11 +1217,11 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
 template <int TA, int TB>
 int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const float* B, int64_t ldb,
            float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, const float* mask,
-           int64_t ldm, cudaStream_t st) {
+           int64_t ldm, const void* a_pre, const void* b_pre, cudaStream_t st) {
   if (!load_encode()) return TL_ERR_UNSUPPORTED;
   if (g_scheme == kSchemeTF32BF16 && g_split_mode == 0)
     return launch_pair<TA, TB>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask,
-                               ldm, st);
+                               ldm, a_pre, b_pre, st);
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
   const int64_t b_rows = TB ? N : K, b_cols = TB ? K : N;
   // the elements a row-major [rows][cols] matrix with leading dim ld spans
@@ -1233,14 +1289,39 @@ bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A,
 
 int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
             const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias, int accumulate,
-            int epilogue, const float* mask, int64_t ldm, cudaStream_t st) {
-  if (!ta && !tb)
-    return launch<0, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
-  if (!ta && tb)
-    return launch<0, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
-  if (ta && !tb)
-    return launch<1, 0>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
-  return launch<1, 1>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, st);
+            int epilogue, const float* mask, int64_t ldm, const void* a_pair, const void* b_pair,
+            cudaStream_t st) {
+#define TL_TC(a, b) \
+  launch<a, b>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask, ldm, a_pair, b_pair, st)
+  if (!ta && !tb) return TL_TC(0, 0);
+  if (!ta && tb) return TL_TC(0, 1);
+  if (ta && !tb) return TL_TC(1, 0);
+  return TL_TC(1, 1);
+#undef TL_TC
+}
+
+bool gemm_uses_pairs(int ta, int tb, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
+  if (g_scheme != kSchemeTF32BF16 || g_split_mode != 0) return false;
+  if (M < 64 || N < 32 || K < 32 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
+  if (lda % 4 || ldb % 4) return false;
+  return lda >= (ta ? M : K) && ldb >= (tb ? K : N);
+}
+
+int64_t pair_bytes(int64_t rows, int64_t cols, int layout) {
+  if (rows <= 0 || cols <= 0) return -1;
+  if (layout == 0) return rows * ((cols + 31) / 32 * 32) * 4;            // K-major
+  if (layout == 1) return ((rows + 31) / 32 * 32) * ((cols + 7) / 8 * 8) * 4;  // MN-major
+  return -1;
+}
+
+int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                 int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st) {
+  const int64_t r_end = mnmajor ? (rows + 31) / 32 * 32 : rows;
+  const int64_t cap = 8LL * sm_count();
+  pair_both_kernel<<<(unsigned)(r_end < cap ? r_end : cap), 256, 0, st>>>(
+      X, ld, rows, cols, reinterpret_cast<__nv_bfloat16*>(kmajor), k_lo_first,
+      reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first);
+  return after_launch();
 }
 
 void gemm_set_split_mode(int mode) { g_split_mode = mode; }

@@ -29,6 +29,7 @@ import numpy as np
 from . import runtime as rt
 from .autograd import BackwardPlanner, Node, grad_name
 from .epilogue import fuse_gemm_epilogues
+from .pairs import plan_gemm_pairs
 from .kernel_generator import KernelGenerator
 from .shapes import Shape, broadcast, complete_env, expr_inputs, numel
 from .steps import EW, Copy, LibCall, Memset0, RegionStep, Step, fuse, kinfo_to_step
@@ -118,12 +119,17 @@ def lower_let(name: str, expr: dict, shapes: Dict[str, Shape], gen: KernelGenera
 
 
 class _Loop(Step):
-    """A ``for`` statement: body phases, rebinds, CUDA-graph replay."""
+    """A ``for`` statement: body phases, rebinds, CUDA-graph replay.
+
+    ``hoisted`` holds steps on values the body never writes (for example the
+    GEMM operand pairs of a loop-invariant input); they run before the body on
+    every eager run and are not part of the captured per-iteration graph."""
 
     def __init__(self, iterations: int, pre: List[Step], bw: List[Step], post: List[Step],
                  rebind: List[Step], label: str):
         self.iterations = int(iterations)
         self.pre, self.bw, self.post, self.rebind = pre, bw, post, rebind
+        self.hoisted: List[Step] = []
         self.label = label
         self.reads = sorted({r for s in self.body() for r in s.reads})
         self.writes = sorted({w for s in self.body() for w in s.writes})
@@ -132,18 +138,25 @@ class _Loop(Step):
     def body(self) -> List[Step]:
         return self.pre + self.bw + self.post + self.rebind
 
+    def steps(self) -> List[Step]:
+        """Everything the loop runs: hoisted steps, then the body."""
+        return self.hoisted + self.body()
+
     def compile(self, P):
-        for s in self.body():
+        for s in self.steps():
             s.compile(P)
 
     def bind(self, P):
+        self._hoisted_calls = [s.bind(P) for s in self.hoisted]
         self._calls = [s.bind(P) for s in self.body()]
         self._stream = P.stream
         self._use_graph = P.use_graphs
         return lambda: self.iterate(self.iterations, first=True)
 
     def run_eager(self):
-        """One iteration, kernel by kernel."""
+        """One iteration, kernel by kernel (after the hoisted steps)."""
+        for c in self._hoisted_calls:
+            c()
         for c in self._calls:
             c()
 
@@ -401,7 +414,7 @@ class Program:
         def walk(lst):
             for s in lst:
                 if isinstance(s, _Loop):
-                    walk(s.body())
+                    walk(s.steps())
                 else:
                     out.append(s)
         walk(self.phase_pre + self.phase_bw + self.phase_post)
@@ -410,6 +423,7 @@ class Program:
     def _fuse_all(self):
         if self.fuse_ops:
             fuse_gemm_epilogues(self)
+            plan_gemm_pairs(self)
         live = set(self.shapes) if self.fetch is None else set(self.fetch)
         live |= set(self.initial)
         live |= {sv["tensor"] for sv in self.saves}
@@ -444,6 +458,7 @@ class Program:
             for s in lst:
                 if isinstance(s, _Loop):
                     flush()
+                    s.hoisted = fz(s.hoisted, s.label + "h")
                     s.pre = fz(s.pre, s.label + "f")
                     s.bw = fz(s.bw, s.label + "b")
                     s.post = fz(s.post, s.label + "p")

@@ -106,6 +106,13 @@ _SIGS = [
     ("tl_gemm_masked", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64,
                                c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_int, c_int,
                                c_void_p, c_int64, c_void_p]),
+    ("tl_gemm_pairs", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64,
+                              c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
+                              c_int, c_int, c_void_p, c_int64, c_void_p]),
+    ("tl_gemm_pair_bytes", c_int64, [c_int64, c_int64, c_int]),
+    ("tl_gemm_pair_prepare", c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
+                                     c_void_p, c_int, c_void_p]),
+    ("tl_gemm_uses_pairs", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_int64, c_int64]),
     ("tl_gemm_path", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                              c_int64, c_void_p, c_int64]),
     ("tl_gemm_force_simt", c_int, [c_int]),

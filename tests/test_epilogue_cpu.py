@@ -70,8 +70,14 @@ def test_second_reader_blocks_relu_fold():
     assert fuse_gemm_epilogues(P) == 0
 
 
+def _masked_gemm(s) -> bool:
+    """A GEMM carrying the relu-mask epilogue (with or without prepared pairs)."""
+    f = getattr(s, "fname", "")
+    return f == "tl_gemm_masked" or (f == "tl_gemm_pairs" and s.args[16][0] == "ptr")
+
+
 def test_engine_runs_the_pass_only_with_fusion_on():
     for fuse_ops, masked in ((False, 0), (True, 2)):
         P = _mlp3(["loss", "W3"], fuse_ops=fuse_ops)
         P._fuse_all()
-        assert sum(getattr(s, "fname", "") == "tl_gemm_masked" for s in _steps(P)) == masked
+        assert sum(_masked_gemm(s) for s in _steps(P)) == masked

@@ -1,8 +1,9 @@
 """GEMM epilogues on the GPU: the relu-mask epilogue (tl_gemm_masked) on every
 GEMM path against a float64 product, and a training program whose relu and
-relu-VJP passes were folded into GEMM epilogues against the same program run
-unfused -- bit-identical, since the folded ops round exactly as the region
-kernels do.  Tolerance for the products: rel 1e-5 of max|C|."""
+relu-VJP passes were folded into GEMM epilogues and whose GEMM operand pairs
+are prepared once per value (pairs.py) against the same program run unfused
+-- bit-identical, since the folded ops round exactly as the region kernels do
+and the prepared pairs equal the per-call ones.  Tolerance for the products: rel 1e-5 of max|C|."""
 import ctypes
 
 import numpy as np
@@ -80,9 +81,13 @@ def test_folded_training_is_bit_identical():
     fetch = ["loss", "W1", "b1", "W2", "b2", "W3", "b3"]
     fused = tl.Program(ast, None, feeds=feeds, fetch=fetch)
     a = fused.run()
-    names = [getattr(s, "fname", "") for s in fused._all_steps()]
+    steps = fused._all_steps()
     fused.free()
-    assert names.count("tl_gemm_masked") == 2
+    masked = [s for s in steps if getattr(s, "fname", "") in ("tl_gemm_masked", "tl_gemm_pairs")
+              and s.args[14 if s.fname == "tl_gemm_masked" else 16][0] == "ptr"]
+    assert len(masked) == 2
+    # operand pairs prepared once per value: x (hoisted), a1, h2's and h1's gradients
+    assert sum(getattr(s, "fname", "") == "tl_gemm_pair_prepare" for s in steps) == 4
     b = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_ops=False).run()
     for k in fetch:
         assert np.array_equal(np.asarray(a[k]), np.asarray(b[k])), k
