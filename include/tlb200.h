@@ -66,6 +66,10 @@ int  tl_memcpy_d2d(void* dst, const void* src, size_t bytes, void* stream);
 int  tl_memset(void* dst, int value, size_t bytes, void* stream);
 
 int  tl_stream_create(void** stream);
+/* A stream whose blocks the GPU schedules first when SMs free up (urgent != 0:
+ * the device's greatest priority), for work that must interleave with long
+ * kernels -- the data-parallel gradient all-reduce.  No reference counterpart. */
+int  tl_stream_create_priority(void** stream, int urgent);
 int  tl_stream_destroy(void* stream);
 int  tl_stream_sync(void* stream);
 int  tl_device_sync(void);

@@ -321,15 +321,9 @@ class BackwardPlanner:
             raise NotImplementedError(f"{node.op} backward for {xs} @ {ws}")
         M, K = xs2
         N = ws[1]
-        if x in self.requires:  # dX[M,K] = G[M,N] @ W^T
-            first = self._first(x)
-            gx = grad_name(x)
-            S.setdefault(gx, xs)
-            self.steps.append(LibCall(f"dX:{gx}", "tl_gemm",
-                                      [("int", 0), ("int", 1), ("int", M), ("int", K), ("int", N),
-                                       ("ptr", g), ("int", N), ("ptr", w), ("int", N), ("ptr", gx),
-                                       ("int", K), ("null",), ("int", 0 if first else 1), ("int", 0)],
-                                      [g, w] + ([] if first else [gx]), [gx]))
+        # parameter gradients (dW, db) first, then dX: in data-parallel training
+        # a layer's weight gradient is then final before the (larger) dX product
+        # of that layer runs, and its all-reduce overlaps that product
         if w in self.requires:  # dW[K,N] = X^T @ G
             first = self._first(w)
             gw = grad_name(w)
@@ -354,6 +348,15 @@ class BackwardPlanner:
                                            ("int", gs[0]), ("int", gs[1]), ("scratch",)], [g], [dst]))
                 if not first:
                     self.steps.append(EW(gb, bs, "add", [("name", gb, "full"), ("name", dst, "full")]))
+        if x in self.requires:  # dX[M,K] = G[M,N] @ W^T
+            first = self._first(x)
+            gx = grad_name(x)
+            S.setdefault(gx, xs)
+            self.steps.append(LibCall(f"dX:{gx}", "tl_gemm",
+                                      [("int", 0), ("int", 1), ("int", M), ("int", K), ("int", N),
+                                       ("ptr", g), ("int", N), ("ptr", w), ("int", N), ("ptr", gx),
+                                       ("int", K), ("null",), ("int", 0 if first else 1), ("int", 0)],
+                                      [g, w] + ([] if first else [gx]), [gx]))
 
     def _vjp_ce(self, node: Node, fused_softmax: set, active: List[Node]):
         """cross_entropy autograd.py:691-704 (+ the softmax VJP when fused)."""

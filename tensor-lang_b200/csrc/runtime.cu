@@ -184,6 +184,16 @@ int tl_stream_create(void** stream) {
   *stream = (void*)s;
   return TL_OK;
 }
+int tl_stream_create_priority(void** stream, int urgent) {
+  if (!stream) return TL_ERR_INVALID_ARG;
+  int least = 0, greatest = 0;
+  TL_CUDA_TRY(cudaDeviceGetStreamPriorityRange(&least, &greatest));
+  cudaStream_t s;
+  TL_CUDA_TRY(cudaStreamCreateWithPriority(&s, cudaStreamNonBlocking, urgent ? greatest : least));
+  *stream = s;
+  return TL_OK;
+}
+
 int tl_stream_destroy(void* stream) {
   TL_CUDA_TRY(cudaStreamDestroy((cudaStream_t)stream));
   return TL_OK;

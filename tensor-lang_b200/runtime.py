@@ -59,6 +59,7 @@ _SIGS = [
     ("tl_memcpy_d2d", c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     ("tl_memset", c_int, [c_void_p, c_int, c_size_t, c_void_p]),
     ("tl_stream_create", c_int, [ctypes.POINTER(c_void_p)]),
+    ("tl_stream_create_priority", c_int, [ctypes.POINTER(c_void_p), c_int]),
     ("tl_stream_destroy", c_int, [c_void_p]),
     ("tl_stream_sync", c_int, [c_void_p]),
     ("tl_device_sync", c_int, []),

@@ -152,7 +152,11 @@ def test_bucket_plan_overlaps_backward():
 
     class _Comm:  # only identity matters to the planner
         handle = stream = None
-    steps, arena = dp.plan_buckets(list(bw), grads, P.shapes, _Comm())
+    single, _ = dp.plan_buckets(list(bw), grads, P.shapes, _Comm(), None)
+    ar = [s for s in single if isinstance(s, dp.AllReduceBucket)]
+    assert len(ar) == 1 and sorted(ar[0].names) == sorted(grads)   # default: one, at the end
+    assert single.index(ar[0]) == len(single) - 2 and isinstance(single[-1], dp.AllReduceJoin)
+    steps, arena = dp.plan_buckets(list(bw), grads, P.shapes, _Comm(), dp.BUCKET_BYTES)
     labels = [s.label for s in steps]
     buckets = [s for s in steps if isinstance(s, dp.AllReduceBucket)]
     assert isinstance(steps[-1], dp.AllReduceJoin)
