@@ -81,3 +81,36 @@ def test_engine_runs_the_pass_only_with_fusion_on():
         P = _mlp3(["loss", "W3"], fuse_ops=fuse_ops)
         P._fuse_all()
         assert sum(_masked_gemm(s) for s in _steps(P)) == masked
+
+
+def test_operand_pairs_planned_once_per_value():
+    """pairs.py: each GEMM operand value gets one pair step (both layouts from
+    one read) right after its producer; the loop-invariant input's pairs are
+    hoisted out of the per-iteration graph; weights rebound in place keep the
+    per-call pre-pass."""
+    tl = load_backend()
+    pr = tl.programs
+    kw = dict(B=4096, I=1024, H=4096, C=10)
+    P = tl.Program(pr.mlp3_train(epochs=2, **kw), None, fetch=["loss", "W3"])
+    P._fuse_all()
+    loop = P.loops[0]
+    assert [s.label for s in loop.hoisted] == ["pairs:x"]
+    assert sorted(loop.hoisted[0].writes) == ["__pair_x_hoist_k0", "__pair_x_hoist_m0"]
+    body = loop.body()
+    labels = [s.label for s in body]
+    prep = {s.label: s for s in body if getattr(s, "fname", "") == "tl_gemm_pair_prepare"}
+    assert sorted(prep) == ["pairs:a1", "pairs:h1_grad", "pairs:h2_grad"]
+    # both layouts from one read where two roles use the value
+    assert len(prep["pairs:a1"].writes) == 2 and len(prep["pairs:h2_grad"].writes) == 2
+    # each pair step directly follows the step that writes its tensor
+    for lab, st in prep.items():
+        x = lab.split(":", 1)[1]
+        i = labels.index(lab)
+        assert x in body[i - 1].writes, (lab, labels[i - 1])
+    users = [s for s in body if getattr(s, "fname", "") == "tl_gemm_pairs"]
+    assert len(users) == 5   # both forward GEMMs, dW2, dX1, dW1 (the 10-wide head has none)
+    for s in users:
+        for name in (s.args[7][1] if s.args[7][0] == "ptr" else None,
+                     s.args[10][1] if s.args[10][0] == "ptr" else None):
+            assert name is None or name.startswith("__pair_")
+    assert not any("W2" in w for s in prep.values() for w in s.writes)

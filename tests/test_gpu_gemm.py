@@ -157,3 +157,46 @@ def test_gemm_explicit_split_mode():
             assert_close(out, ref, 1e-5, "explicit split")
     finally:
         L.tl_gemm_force_simt(0)
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(300, 520, 200), (1000, 264, 1000)])
+def test_prepared_pairs_match_per_call_pairs(ta, tb, M, N, K):
+    """Pairs from tl_gemm_pair_prepare (both layouts from one read, ragged
+    shapes: padding rows and columns) give the same product, bit for bit, as
+    the pairs tl_gemm computes itself."""
+    tl = load_backend()
+    rt = tl.runtime
+    L = rt.lib()
+    dev = rt.Device.get(0)
+    rng = np.random.default_rng(M + N + K + ta + 2 * tb)
+    A = rng.standard_normal((K, M) if ta else (M, K)).astype(np.float32)
+    B = rng.standard_normal((N, K) if tb else (K, N)).astype(np.float32)
+    dA, dB = rt.DeviceBuffer(dev, A.shape), rt.DeviceBuffer(dev, B.shape)
+    dA.upload(A)
+    dB.upload(B)
+    lda, ldb = A.shape[1], B.shape[1]
+    assert L.tl_gemm_uses_pairs(ta, tb, M, N, K, lda, ldb) == 1
+    # the layout each operand needs (include/tlb200.h), and both layouts of A
+    a_layout, b_layout = (1 if ta else 0), (0 if tb else 1)
+    pk = rt.DeviceBuffer(dev, (L.tl_gemm_pair_bytes(*A.shape, 0) // 4,))
+    pm = rt.DeviceBuffer(dev, (L.tl_gemm_pair_bytes(*A.shape, 1) // 4,))
+    pb = rt.DeviceBuffer(dev, (L.tl_gemm_pair_bytes(*B.shape, b_layout) // 4,))
+    rt.check(L.tl_gemm_pair_prepare(dA.ptr, lda, A.shape[0], A.shape[1], pk.ptr, 0, pm.ptr, 0,
+                                    dev.stream))
+    rt.check(L.tl_gemm_pair_prepare(dB.ptr, ldb, B.shape[0], B.shape[1],
+                                    pb.ptr if b_layout == 0 else None, 1,
+                                    pb.ptr if b_layout == 1 else None, 1, dev.stream))
+    pa = pm if a_layout == 1 else pk
+    dC1, dC2 = rt.DeviceBuffer(dev, (M, N)), rt.DeviceBuffer(dev, (M, N))
+    rt.check(L.tl_gemm(ta, tb, M, N, K, dA.ptr, lda, dB.ptr, ldb, dC1.ptr, N, None, 0, 0,
+                       dev.stream))
+    rt.check(L.tl_gemm_pairs(ta, tb, M, N, K, dA.ptr, lda, pa.ptr, dB.ptr, ldb, pb.ptr, dC2.ptr, N,
+                             None, 0, 0, None, 0, dev.stream))
+    c1, c2 = dC1.download(), dC2.download()
+    for b in (dA, dB, pk, pm, pb, dC1, dC2):
+        b.free()
+    assert np.array_equal(c1, c2)
+    ref = (A.astype(np.float64).T if ta else A.astype(np.float64)) @ \
+        (B.astype(np.float64).T if tb else B.astype(np.float64))
+    assert_close(c2, ref, 1e-5, f"prepared pairs {ta}{tb} {M}x{N}x{K}")
