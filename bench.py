@@ -24,6 +24,7 @@ and autograd) on the host cores instead.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import os
 import subprocess
@@ -181,6 +182,65 @@ def time_events(tl, stream, fn, reps):
     return e0.elapsed_ms(e1) / reps
 
 
+def e2e_time(tl, dev, loop, stream, px, pt, pl, xs, ts, steps):
+    """Milliseconds per training step with every batch uploaded from pinned host
+    memory and every loss read back to the host.
+
+    Step i+1's batch is copied host->device on a separate copy stream into
+    staging buffers while step i computes; step i+1 then moves it into place
+    with a device-to-device copy, re-prepares the hoisted operands of the
+    (new) batch and replays the iteration graph.  The timed region holds
+    exactly ``steps`` host->device batch copies and ``steps`` loss reads; the
+    first upload is not overlapped with anything."""
+    rt = tl.runtime
+    L = rt.lib()
+    hx, ht, hl = rt.PinnedHost(xs.nbytes), rt.PinnedHost(ts.nbytes), rt.PinnedHost(4)
+    hx.array(xs.shape)[...] = xs
+    ht.array(ts.shape)[...] = ts
+    sx, st = rt.DeviceBuffer(dev, xs.shape), rt.DeviceBuffer(dev, ts.shape)
+    cs = ctypes.c_void_p()
+    rt.check(L.tl_stream_create(ctypes.byref(cs)), "copy stream")
+    copy = cs.value
+    start, end, ready, consumed = rt.Event(), rt.Event(), rt.Event(), rt.Event()
+
+    def upload():
+        rt.check(L.tl_memcpy_h2d(sx.ptr, hx.ptr, xs.nbytes, copy), "h2d x")
+        rt.check(L.tl_memcpy_h2d(st.ptr, ht.ptr, ts.nbytes, copy), "h2d t")
+        ready.record(copy)
+
+    def step(prefetch):
+        rt.check(L.tl_stream_wait_event(stream, ready.ptr), "wait batch")
+        rt.check(L.tl_memcpy_d2d(px, sx.ptr, xs.nbytes, stream), "d2d x")
+        rt.check(L.tl_memcpy_d2d(pt, st.ptr, ts.nbytes, stream), "d2d t")
+        consumed.record(stream)
+        if prefetch:  # the next batch streams in while this step computes
+            rt.check(L.tl_stream_wait_event(copy, consumed.ptr), "wait staging")
+            upload()
+        loop.run_hoisted()
+        loop.replay(1)
+        rt.check(L.tl_memcpy_d2h(hl.ptr, pl, 4, stream), "d2h loss")
+
+    def run(n):
+        start.record(stream)
+        rt.check(L.tl_stream_wait_event(copy, start.ptr), "wait start")
+        upload()
+        for i in range(n):
+            step(i + 1 < n)
+        end.record(stream)
+        rt.check(L.tl_stream_sync(stream), "sync")
+        return start.elapsed_ms(end) / n
+
+    try:
+        run(2)  # untimed: warms the copy path
+        return run(steps)
+    finally:
+        rt.check(L.tl_stream_sync(copy), "sync copy")
+        L.tl_stream_destroy(copy)
+        hx.free()
+        ht.free()
+        hl.free()
+
+
 def fused_op_bench(tl, dev, reps=20):
     """The fused elementwise chain on [8192,8192], GB/s of algorithmic traffic."""
     pr = tl.programs
@@ -251,27 +311,14 @@ def run_ours(args, rank, world, local):
     rdv.barrier()
     all_ms = rdv.gather(ms)
 
-    # e2e through the public API: host (pinned) inputs uploaded every step,
-    # the loss read back every step
+    # e2e through the public API: every step's batch comes from pinned host
+    # memory and every step's loss goes back to the host
     xs, ts = feeds["x"], feeds["t"]
-    hx = rt.PinnedHost(xs.nbytes)
-    hx.array(xs.shape)[...] = xs
-    ht = rt.PinnedHost(ts.nbytes)
-    ht.array(ts.shape)[...] = ts
-    hl = rt.PinnedHost(4)
     L = rt.lib()
-    px, pt, pl = P.ptr("x"), P.ptr("t"), P.ptr("loss")
-
-    def e2e_step():
-        rt.check(L.tl_memcpy_h2d(px, hx.ptr, xs.nbytes, stream), "h2d x")
-        rt.check(L.tl_memcpy_h2d(pt, ht.ptr, ts.nbytes, stream), "h2d t")
-        loop.replay(1)
-        rt.check(L.tl_memcpy_d2h(hl.ptr, pl, 4, stream), "d2h loss")
-
-    e2e_step()
-    P.sync()
+    e2e_steps = max(1, min(args.steps, 10))
+    e2e_ms = e2e_time(tl, rt.Device.get(dev), loop, stream, P.ptr("x"), P.ptr("t"), P.ptr("loss"),
+                      xs, ts, e2e_steps)
     rdv.barrier()
-    e2e_ms = time_events(tl, stream, e2e_step, max(1, min(args.steps, 10)))
     all_e2e = rdv.gather(e2e_ms)
 
     # dominant kernel: the hidden-layer GEMM (b x 4096 x 4096), timed alone
@@ -339,7 +386,8 @@ def run_ours(args, rank, world, local):
 
 def run_micro(args):
     """One kernel alone, for profiling and per-kernel rooflines:
-    gemm        65536/8 x 4096 x 4096 linear forward (A 128 MiB, B 64 MiB)
+    gemm        M x 4096 x 4096 linear forward (--gemm-m, default 8192:
+                A 128 MiB, B 64 MiB; 65536 is the training step's hidden GEMM)
     fused       the [8192,8192] fused elementwise chain
     softmax     softmax over rows of [16384,4096]
     rowsum      sum over rows of [16384,4096]
@@ -376,7 +424,7 @@ def run_micro(args):
         P.free()
         return 0
     if args.micro == "gemm":
-        M, N, K = 8192, 4096, 4096
+        M, N, K = args.gemm_m, 4096, 4096
         rng = np.random.default_rng(0)
         A = rt.DeviceBuffer(dev, (M, K))
         A.upload(rng.standard_normal((M, K), dtype=np.float32))
@@ -425,6 +473,7 @@ def main():
     ap.add_argument("--cpu-rows", type=int, default=4096)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fused", action="store_true")
+    ap.add_argument("--gemm-m", type=int, default=8192, help="rows of the --micro gemm product")
     ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum", "reductions"],
                     default=None,
                     help="time one kernel alone (profiling aid); prints its own JSON line")

@@ -153,10 +153,15 @@ class _Loop(Step):
         self._use_graph = P.use_graphs
         return lambda: self.iterate(self.iterations, first=True)
 
-    def run_eager(self):
-        """One iteration, kernel by kernel (after the hoisted steps)."""
+    def run_hoisted(self):
+        """Re-run the hoisted steps, for a caller that has rewritten a
+        loop-invariant input (a new batch) between iterations."""
         for c in self._hoisted_calls:
             c()
+
+    def run_eager(self):
+        """One iteration, kernel by kernel (after the hoisted steps)."""
+        self.run_hoisted()
         for c in self._calls:
             c()
 
