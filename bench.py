@@ -42,9 +42,21 @@ B_GLOBAL, D_IN, D_H, N_CLS = 65536, 1024, 4096, 10
 FLOP_PER_STEP = 7_712_686_521_792  # fwd 3 GEMMs + dW 3 + dX of layers 2,3
 FUSED_N = 8192
 FUSED_BYTES = 805_371_904  # read x, write y and m, plus s and b
+# GEMM operand schemes (tl_gemm_set_scheme): code, description, and bf16
+# MMA-times per fp32 product -- the scheme's ceiling is the bf16 peak / that
+GEMM_SCHEMES = {
+    "bf16x3": (2, "tcgen05 BF16X3: a0*b0 plus one bf16 pair MMA for a0*b1 + a1*b0", 3),
+    "tf32bf16": (1, "tcgen05 split-TF32: TF32 hi*hi plus one bf16 pair MMA for the corrections", 4),
+    "3xtf32": (0, "tcgen05 split-TF32: TF32 hi*hi + hi*lo + lo*hi", 6),
+}
 # DRAM bytes (read + written) of one hidden-layer GEMM kernel launch
-# (65536 x 4096 x 4096, CTA pairs), from an ncu capture; None until measured
-GEMM_TRAFFIC_BYTES = None
+# (65536 x 4096 x 4096, CTA pairs) per scheme, from a one-pass ncu capture of
+# `bench.py --micro gemm --gemm-m 65536`; None where not captured
+GEMM_TRAFFIC_BYTES = {"tf32bf16": 10_070_651_136 + 1_101_682_176}
+
+
+def set_gemm_scheme(tl, name):
+    tl.runtime.check(tl.runtime.lib().tl_gemm_set_scheme(GEMM_SCHEMES[name][0], None), "gemm scheme")
 
 
 def peaks():
@@ -268,6 +280,7 @@ def run_ours(args, rank, world, local):
     from __graft_entry__ import load_package
     tl = load_package()
     rt = tl.runtime
+    set_gemm_scheme(tl, args.gemm_scheme)
     from tensor_lang_b200 import dp
 
     dev = local
@@ -329,7 +342,7 @@ def run_ours(args, rank, world, local):
     P.sync()
     g_ms = time_events(tl, stream, gemm, 5)
     on_tc = L.tl_gemm_path(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("a2"), N) == 0
-    path = ("tcgen05 split-TF32: TF32 hi*hi + bf16 pair corrections, CTA-pair 256x256 tiles"
+    path = (f"{GEMM_SCHEMES[args.gemm_scheme][1]}, CTA-pair 256x256 tiles"
             if on_tc else "CUDA-core fp32")
     loss = float(P.read("loss").reshape(-1)[0])
 
@@ -347,6 +360,7 @@ def run_ours(args, rank, world, local):
                              f"scaled x{B_GLOBAL // rows}"}
         ms_max = max(all_ms)
         hbm, bf16, bf16s, src = peaks()
+        ceiling = bf16 / GEMM_SCHEMES[args.gemm_scheme][2]
         tflops = 2.0 * M * N * K / (g_ms * 1e-3) / 1e12
         line = {
             "metric": "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)",
@@ -360,14 +374,15 @@ def run_ours(args, rank, world, local):
             "model_tflops": FLOP_PER_STEP / (ms_max * 1e-3) / 1e12,
             "loss_rank0": loss,
             # the GEMM call (bf16 pair pre-passes + tcgen05 kernel), fp32-equivalent
-            # flops; per fp32 product the scheme issues one TF32 product (half the
-            # bf16 rate) and two bf16 products, so its ceiling is bf16 / 4
+            # flops; per fp32 product BF16X3 issues three bf16 products (ceiling
+            # bf16 / 3), TF32+bf16 one TF32 product at half the bf16 rate and two
+            # bf16 products (bf16 / 4)
             "roofline": {"bound": "tensor", "kernel": f"GEMM {M}x{N}x{K} ({path})",
                          "achieved": tflops, "peak": bf16, "unit": "TFLOP/s",
                          "frac": tflops / bf16, "peak_source": f"{src} bf16 dense (burst)",
-                         "traffic": GEMM_TRAFFIC_BYTES,
-                         "scheme_ceiling": bf16 / 4,
-                         "frac_of_scheme_ceiling": tflops / (bf16 / 4)},
+                         "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_scheme),
+                         "scheme_ceiling": ceiling,
+                         "frac_of_scheme_ceiling": tflops / ceiling},
             "e2e": {"value": 1000.0 / max(all_e2e), "unit": "steps/s",
                     "h2d_bytes_per_step": int(xs.nbytes + ts.nbytes) * world,
                     "d2h_bytes_per_step": 4 * world},
@@ -401,6 +416,7 @@ def run_micro(args):
     L = rt.lib()
     dev = rt.Device.get(0)
     st = dev.stream
+    set_gemm_scheme(tl, args.gemm_scheme)
     hbm, bf16, _, src = peaks()
     reps = args.steps
     if args.micro == "reductions":
@@ -474,6 +490,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-fused", action="store_true")
     ap.add_argument("--gemm-m", type=int, default=8192, help="rows of the --micro gemm product")
+    ap.add_argument("--gemm-scheme", choices=sorted(GEMM_SCHEMES), default="bf16x3",
+                    help="tensor-core operand scheme of the fp32 GEMMs")
     ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum", "reductions"],
                     default=None,
                     help="time one kernel alone (profiling aid); prints its own JSON line")

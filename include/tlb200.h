@@ -210,7 +210,8 @@ int  tl_concat_rows(const float* a, const float* b, float* out, int64_t rows_a,
  * elements of the row-major storage.  f32 in, f32 out.  On sm_100a the
  * product runs on tcgen05 tensor cores as split-TF32 (three TF32 products
  * hi*hi + hi*lo + lo*hi with fp32 accumulation in tensor memory), which
- * keeps fp32-level accuracy; skinny products (N <= 32, or K <= 32 with B
+ * keeps fp32-level accuracy (the default operand scheme splits each operand
+ * into two bf16 terms instead; see tl_gemm_set_scheme); skinny products (N <= 32, or K <= 32 with B
  * transposed) take bandwidth-bound CUDA-core kernels; other shapes the TMA
  * path cannot describe take a tiled fp32 CUDA-core path.
  * epilogue: 0 none, 1 relu (y = max(0, y)).
@@ -232,9 +233,10 @@ int  tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                     const float* A, int64_t lda, const float* B, int64_t ldb,
                     float* C, int64_t ldc, const float* bias, int accumulate, int epilogue,
                     const float* mask, int64_t ldm, void* stream);
-/* Precomputed bf16 pair matrices for the TF32+bf16 scheme (no reference
- * counterpart).  The scheme multiplies hi*hi on TF32 and the corrections on
- * a pair matrix per operand; tl_gemm computes those pairs itself on every
+/* Precomputed bf16 pair matrices for the TF32+bf16 and BF16X3 schemes (no
+ * reference counterpart).  Both multiply on a pair matrix per operand (bf16
+ * values beside bf16 lows; the low part depends on the scheme selected when
+ * the pair is prepared); tl_gemm computes those pairs itself on every
  * call.  A caller that uses one operand in several products, or the same
  * operand over many calls, prepares its pairs once:
  *   tl_gemm_pair_bytes(rows, cols, layout)   bytes of the pair of X[rows][cols]
@@ -247,7 +249,7 @@ int  tl_gemm_masked(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
  *     tl_gemm_masked taking those pairs (null: computed inside as usual).
  *     The layout an operand needs: A as stored (trans_a 0) -> K-major, A^T
  *     (trans_a 1) -> MN-major; B^T as stored (trans_b 1) -> K-major, B
- *     (trans_b 0) -> MN-major.  Paths other than the TF32+bf16 tensor-core
+ *     (trans_b 0) -> MN-major.  Paths other than the pair-scheme tensor-core
  *     path ignore the pairs.
  *   tl_gemm_uses_pairs(ta, tb, M, N, K, lda, ldb)  1 if such a call takes
  *     that path (so prepared pairs are used), else 0; depends only on the
@@ -277,12 +279,21 @@ int  tl_gemm_force_simt(int force);
  * the reference calls cuBLAS SGEMM / its own fp32 kernels).
  *   TL_GEMM_3XTF32     hi*hi + hi*lo + lo*hi, three TF32 MMAs per k-step
  *   TL_GEMM_TF32_BF16  hi*hi on TF32, both correction terms in one bf16 MMA
- *                      over [bf16(A)|bf16(loA)] . [bf16(loB)|bf16(B)] (default)
- * Both stay within rel 1e-5 of an fp64 product on N(0,1) data.  Returns
+ *                      over [bf16(A)|bf16(loA)] . [bf16(loB)|bf16(B)]
+ *   TL_GEMM_BF16X3     all bf16: a = a0 + a1 with a0 = bf16(a), a1 =
+ *                      bf16(a - a0); a0*b0 plus one pair MMA over
+ *                      [a0|a1] . [b1|b0]; operands are read only as pairs
+ *                      (default: 3 bf16 MMA-times per product against 4,
+ *                      half the operand bytes; max rel err ~5e-6 against
+ *                      ~1.6e-6)
+ * All stay within rel 1e-5 of an fp64 product on N(0,1) data.  Returns
  * TL_ERR_INVALID_ARG for an unknown scheme; *previous (if non-null) receives
- * the scheme that was in force.  Applies to launches made after the call. */
+ * the scheme that was in force.  Applies to launches made after the call;
+ * pair matrices (tl_gemm_pair_prepare) are scheme-specific, so switch the
+ * scheme before preparing a program, not between its launches. */
 #define TL_GEMM_3XTF32 0
 #define TL_GEMM_TF32_BF16 1
+#define TL_GEMM_BF16X3 2
 int  tl_gemm_set_scheme(int scheme, int* previous);
 /* Tile shape of the tensor-core path (no reference counterpart).  enable = 1
  * (default): products with more than 128 rows use 256 x 256 tiles computed by

@@ -1,5 +1,5 @@
-// Split-TF32 GEMM on the sm_100a tensor cores: tcgen05.mma with the
-// accumulator in tensor memory, operands staged by TMA.
+// Split-precision fp32 GEMM on the sm_100a tensor cores: tcgen05.mma with
+// the accumulator in tensor memory, operands staged by TMA.
 //
 // Serves matmul (kernel_generator.py:501-525), linear (:1584-1661) and the
 // matmul/linear VJPs (autograd.py:520-537, 619-646), in float32:
@@ -12,7 +12,7 @@
 // lo*hi, accumulating in fp32 in TMEM (the dropped lo*lo term is ~2^-22
 // relative).
 //
-// The TF32+bf16 scheme (the default) keeps hi*hi on the TF32 path and folds
+// The TF32+bf16 scheme keeps hi*hi on the TF32 path and folds
 // both correction terms into one bf16 MMA over a K-concatenated pair:
 //   [bf16(A) | bf16(loA)] . [bf16(loB) | bf16(B)]  =  A*loB + loA*B  (+ ~2^-19)
 // A pre-pass writes each operand's pair matrix in the operand's own major
@@ -23,6 +23,17 @@
 // TF32 MMA plus half a bf16 MMA of the same shape: 2 TF32 MMA-times instead of
 // 3.  Per product the error is below 9 * 2^-20 relative (lo*lo dropped,
 // bf16 rounding of the correction operands).
+//
+// The BF16X3 scheme (the default) splits each operand into two bf16 terms,
+// a = a0 + a1 with a0 = bf16(a) and a1 = bf16(a - a0) (16 significant bits),
+// and keeps the three leading products a0*b0 + a0*b1 + a1*b0: a0*b0 reads
+// the value halves of the pair tiles, and the pair MMA over [a0|a1].[b1|b0]
+// adds both cross terms, so the fp32 operands are never loaded.  Per
+// 32-deep k-block the tensor core does 3 bf16 MMA-times (TF32+bf16: 4) and a
+// CTA loads 32 KB (TF32+bf16: 64 KB).  Per product the error is below
+// ~3 * 2^-16 relative (a1*b1 dropped, bf16 rounding of a1 and b1); measured
+// on N(0,1) data at K = 4096-65536: max 5e-6 relative to max|C|, against
+// 1.6e-6 for TF32+bf16.
 //
 // One CTA computes a 128 x 256 tile with 10 warps:
 //   warp 0 lane 0   TMA producer (2-stage ring of hi/lo tiles of A and B)
@@ -131,12 +142,12 @@ __device__ __forceinline__ void mma_tf32(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                         uint32_t idesc) {
+                                         uint32_t idesc, uint32_t accumulate = 1u) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 1, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
@@ -231,6 +242,7 @@ __device__ __forceinline__ uint64_t mn16_desc(uint32_t tile, int k) {
 // Operand schemes
 constexpr int kScheme3xTF32 = 0;    // lo tiles fp32: hi*hi + hi*lo + lo*hi, all TF32
 constexpr int kSchemeTF32BF16 = 1;  // pair tiles bf16: hi*hi TF32 + one bf16 pair MMA
+constexpr int kSchemeBF16X3 = 2;    // pair tiles only: v*v + one bf16 pair MMA, all bf16
 
 struct Params {
   int M, N, K;
@@ -329,7 +341,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAlo,
                    const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBlo,
                    Params p) {
-  constexpr bool PAIR = SCHEME == kSchemeTF32BF16;
+  constexpr bool PAIR = SCHEME != kScheme3xTF32;  // bf16 pair tiles
+  constexpr bool X3 = SCHEME == kSchemeBF16X3;    // pair tiles only, no fp32 tiles
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
   uint64_t* bars = (uint64_t*)(smem + STAGES * STAGE_BYTES);
@@ -379,9 +392,12 @@ __global__ void __launch_bounds__(THREADS, 1)
         const uint32_t sA = smem_u32(st), sAl = sA + A_TILE;
         const uint32_t sB = sAl + A_TILE, sBl = sB + B_TILE;
         const uint32_t fb = smem_u32(&full[s]);
-        mbar_expect_tx(fb, STAGE_BYTES);
+        // the bf16 pair tiles are as large as the fp32 tiles (A_TILE, B_TILE)
+        mbar_expect_tx(fb, X3 ? A_TILE + B_TILE : STAGE_BYTES);
         const int k0 = kb * BK;
-        if (TA == 0) {
+        if (X3) {
+          // no fp32 tiles
+        } else if (TA == 0) {
           tma_load_2d(sA, &tmA, fb, k0, m0);
           if (!PAIR) tma_load_2d(sAl, &tmAlo, fb, k0, m0);
         } else {
@@ -391,7 +407,9 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!PAIR) tma_load_2d(sAl + c * 4096, &tmAlo, fb, m0 + 32 * c, k0);
           }
         }
-        if (TB == 1) {
+        if (X3) {
+          // no fp32 tiles
+        } else if (TB == 1) {
           tma_load_2d(sB, &tmB, fb, k0, n0);
           if (!PAIR) tma_load_2d(sBl, &tmBlo, fb, k0, n0);
         } else {
@@ -442,7 +460,17 @@ __global__ void __launch_bounds__(THREADS, 1)
           unsigned char* st = smem + s * STAGE_BYTES;
           const uint32_t sA = smem_u32(st), sAl = sA + A_TILE;
           const uint32_t sB = sAl + A_TILE, sBl = sB + B_TILE;
-          if constexpr (PAIR) {
+          if constexpr (X3) {
+            // values x values: the A pair's first half (k-steps 0, 1) with
+            // the B pair's second half (k-steps 2, 3; B pairs hold lows first)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma_bf16(acc, TA ? mn16_desc(sAl, k) : kmajor_desc(sAl, k),
+                       TB ? kmajor_desc(sBl, k + 2) : mn16_desc(sBl, k + 2),
+                       idesc_bf16<TA, TB ? 0 : 1>(), first);
+            }
+          } else if constexpr (PAIR) {
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k) {
               const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
@@ -450,6 +478,8 @@ __global__ void __launch_bounds__(THREADS, 1)
               const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
               mma_tf32(acc, a, bh, idesc, first);
             }
+          }
+          if constexpr (PAIR) {
             // 64 bf16 per row (32 values, 32 lows): 4 k-steps of 16, each a 32-byte advance
 #pragma unroll
             for (int k = 0; k < 4; ++k)
@@ -536,6 +566,15 @@ constexpr int HB = 128;                            // B rows (N) held per CTA
 constexpr int B_HALF = HB * BK * 4;                // 16 KB
 constexpr int STAGE2_BYTES = 2 * A_TILE + 2 * B_HALF;  // 64 KB per CTA
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+// The BF16X3 scheme stages only the two pair tiles (32 KB per CTA), so twice
+// as many stages fit in the same shared memory.
+template <int SCHEME>
+struct Ring2 {
+  static constexpr bool X3 = SCHEME == kSchemeBF16X3;
+  static constexpr int kBytes = X3 ? 2 * A_TILE : STAGE2_BYTES;
+  static constexpr int kStages = X3 ? 2 * STAGES2 : STAGES2;
+  static_assert(kBytes * kStages == STAGE2_BYTES * STAGES2, "ring fits the allocation");
+};
 
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
@@ -572,12 +611,12 @@ __device__ __forceinline__ void mma2_tf32(uint32_t d_tmem, uint64_t a_desc, uint
       : "memory");
 }
 __device__ __forceinline__ void mma2_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
-                                          uint32_t idesc) {
+                                          uint32_t idesc, uint32_t accumulate = 1u) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, 1, 0;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc)
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
 // arrive on the barrier at this shared offset in both CTAs of the pair once
@@ -606,13 +645,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAx,
                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBx,
                     Params p) {
-  constexpr bool PAIR = SCHEME == kSchemeTF32BF16;
+  constexpr bool PAIR = SCHEME != kScheme3xTF32;  // bf16 pair tiles
+  constexpr bool X3 = Ring2<SCHEME>::X3;          // pair tiles only, no fp32 tiles
+  constexpr int NST = Ring2<SCHEME>::kStages, SBYTES = Ring2<SCHEME>::kBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + STAGES2 * STAGE2_BYTES);
-  uint64_t* full = bars;                    // [STAGES2] loads of both CTAs -> leader's MMA
-  uint64_t* empty = bars + STAGES2;         // [STAGES2] MMA -> each CTA's producer
-  uint64_t* acc_full = bars + 2 * STAGES2;  // [2] MMA -> each CTA's epilogue
+  uint64_t* bars = (uint64_t*)(smem + NST * SBYTES);
+  uint64_t* full = bars;                // [NST] loads of both CTAs -> leader's MMA
+  uint64_t* empty = bars + NST;         // [NST] MMA -> each CTA's producer
+  uint64_t* acc_full = bars + 2 * NST;  // [2] MMA -> each CTA's epilogue
   uint64_t* acc_free = acc_full + 2;        // [2] both CTAs' epilogues -> leader's MMA
   uint32_t* tmem_slot = (uint32_t*)(acc_free + 2);
 
@@ -633,7 +674,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int nchunks = (nk + KC - 1) / KC;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES2; ++s) {
+    for (int s = 0; s < NST; ++s) {
       mbar_init(smem_u32(&full[s]), 1);
       mbar_init(smem_u32(&empty[s]), 1);
     }
@@ -661,16 +702,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (lane == 0) {
       const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the leader's full[0]
       for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % STAGES2;
-        const uint32_t ph = (kb / STAGES2) & 1;
-        if (kb >= STAGES2 && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) break;
-        unsigned char* st = smem + s * STAGE2_BYTES;
-        const uint32_t sA = smem_u32(st), sAx = sA + A_TILE;
-        const uint32_t sB = sAx + A_TILE, sBx = sB + B_HALF;
+        const int s = kb % NST;
+        const uint32_t ph = (kb / NST) & 1;
+        if (kb >= NST && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) break;
+        unsigned char* st = smem + s * SBYTES;
+        const uint32_t s0 = smem_u32(st);
+        // X3 stage: A pair, B pair; otherwise A, A pair (or lo), B, B pair (or lo)
+        const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
+        const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
         const uint32_t fb = full0 + 8u * (uint32_t)s;
-        if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * STAGE2_BYTES);
+        if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * SBYTES);
         const int k0 = (kb0 + kb) * BK;
-        if (TA == 0) {
+        if (X3) {
+          // no fp32 tiles
+        } else if (TA == 0) {
           tma_load_2d_pair(sA, &tmA, fb, k0, m0);
           if (!PAIR) tma_load_2d_pair(sAx, &tmAx, fb, k0, m0);
         } else {
@@ -680,7 +725,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             if (!PAIR) tma_load_2d_pair(sAx + c * 4096, &tmAx, fb, m0 + 32 * c, k0);
           }
         }
-        if (TB == 1) {
+        if (X3) {
+          // no fp32 tiles
+        } else if (TB == 1) {
           tma_load_2d_pair(sB, &tmB, fb, k0, nb);
           if (!PAIR) tma_load_2d_pair(sBx, &tmBx, fb, k0, nb);
         } else {
@@ -721,17 +768,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         fence_after();
         const int kb_end = min(nk, (c + 1) * KC);
         for (int kb = c * KC; kb < kb_end; ++kb) {
-          const int s = kb % STAGES2;
-          const uint32_t ph = (kb / STAGES2) & 1;
+          const int s = kb % NST;
+          const uint32_t ph = (kb / NST) & 1;
           if (!mbar_wait(smem_u32(&full[s]), ph)) {
             ok = false;
             break;
           }
           fence_after();
-          unsigned char* st = smem + s * STAGE2_BYTES;
-          const uint32_t sA = smem_u32(st), sAx = sA + A_TILE;
-          const uint32_t sB = sAx + A_TILE, sBx = sB + B_HALF;
-          if constexpr (PAIR) {
+          unsigned char* st = smem + s * SBYTES;
+          const uint32_t s0 = smem_u32(st);
+          const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
+          const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
+          if constexpr (X3) {
+            // values x values: the A pair's first half (k-steps 0, 1) with
+            // the B pair's second half (k-steps 2, 3; B pairs hold lows first)
+#pragma unroll
+            for (int k = 0; k < 2; ++k) {
+              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+              mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
+                        TB ? kmajor_desc(sBx, k + 2) : mn16_desc(sBx, k + 2),
+                        idesc2_bf16<TA, TB ? 0 : 1>(), first);
+            }
+          } else if constexpr (PAIR) {
 #pragma unroll
             for (int k = 0; k < BK / 8; ++k) {
               const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
@@ -739,6 +797,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
               mma2_tf32(acc, a, bh, idesc, first);
             }
+          }
+          if constexpr (PAIR) {
 #pragma unroll
             for (int k = 0; k < 4; ++k)
               mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
@@ -889,8 +949,13 @@ __global__ void __launch_bounds__(256) split_lo_kernel(const float* __restrict__
     dst[i] = src[i] - __uint_as_float(__float_as_uint(src[i]) & 0xFFFFE000u);
 }
 
-__device__ __forceinline__ float lo_of(float x) {
-  return x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
+// The low part a pair matrix stores beside bf16(x): for the TF32+bf16 scheme
+// (lo_mode 0) x - trunc_tf32(x), the part the TF32 product misses; for the
+// BF16X3 scheme (lo_mode 1) x - bf16(x), the part the bf16 value misses.
+// Both differences are exact in fp32.
+__device__ __forceinline__ float lo_of(float x, int lo_mode) {
+  return lo_mode ? x - __bfloat162float(__float2bfloat16_rn(x))
+                 : x - __uint_as_float(__float_as_uint(x) & 0xFFFFE000u);
 }
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return (uint32_t)__bfloat16_as_ushort(__float2bfloat16_rn(a)) |
@@ -904,7 +969,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
 // groups of a row are spread over the threads.
 __global__ void __launch_bounds__(256) pair_rows_kernel(const float* __restrict__ X, int64_t ld,
                                                         int64_t R, int64_t K, int64_t kp,
-                                                        int lo_first, __nv_bfloat16* __restrict__ P) {
+                                                        int lo_first, int lo_mode,
+                                                        __nv_bfloat16* __restrict__ P) {
   const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
   const int64_t nq = kp >> 2;
   for (int64_t r = blockIdx.x; r < R; r += gridDim.x) {
@@ -921,7 +987,8 @@ __global__ void __launch_bounds__(256) pair_rows_kernel(const float* __restrict_
         for (int i = 0; i < 4; ++i) x[i] = (k + i < K) ? src[k + i] : 0.f;
       }
       const uint2 hv = make_uint2(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]));
-      const uint2 lv = make_uint2(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])));
+      const uint2 lv = make_uint2(pack_bf16(lo_of(x[0], lo_mode), lo_of(x[1], lo_mode)),
+                                  pack_bf16(lo_of(x[2], lo_mode), lo_of(x[3], lo_mode)));
       __nv_bfloat16* o = dst + 64 * (k >> 5) + (k & 31);
       *reinterpret_cast<uint2*>(o) = lo_first ? lv : hv;
       *reinterpret_cast<uint2*>(o + 32) = lo_first ? hv : lv;
@@ -937,7 +1004,8 @@ __global__ void __launch_bounds__(256) pair_rows_kernel(const float* __restrict_
 // one k row.
 __global__ void __launch_bounds__(256) pair_mn_kernel(const float* __restrict__ X, int64_t ld,
                                                       int64_t K, int64_t R, int64_t rp, int64_t kp,
-                                                      int lo_first, __nv_bfloat16* __restrict__ P) {
+                                                      int lo_first, int lo_mode,
+                                                      __nv_bfloat16* __restrict__ P) {
   const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
   const int64_t ng = rp >> 3;
   for (int64_t k = blockIdx.x; k < kp; k += gridDim.x) {
@@ -957,8 +1025,10 @@ __global__ void __launch_bounds__(256) pair_mn_kernel(const float* __restrict__ 
       }
       const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
                                   pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
-      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])),
-                                  pack_bf16(lo_of(x[4]), lo_of(x[5])), pack_bf16(lo_of(x[6]), lo_of(x[7])));
+      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0], lo_mode), lo_of(x[1], lo_mode)),
+                                  pack_bf16(lo_of(x[2], lo_mode), lo_of(x[3], lo_mode)),
+                                  pack_bf16(lo_of(x[4], lo_mode), lo_of(x[5], lo_mode)),
+                                  pack_bf16(lo_of(x[6], lo_mode), lo_of(x[7], lo_mode)));
       *reinterpret_cast<uint4*>(vrow + r) = lo_first ? lv : hv;
       *reinterpret_cast<uint4*>(lrow + r) = lo_first ? hv : lv;
     }
@@ -974,7 +1044,8 @@ __global__ void __launch_bounds__(256) pair_mn_kernel(const float* __restrict__ 
 __global__ void __launch_bounds__(256) pair_both_kernel(const float* __restrict__ X, int64_t ld,
                                                         int64_t R, int64_t C,
                                                         __nv_bfloat16* __restrict__ pk, int k_lo_first,
-                                                        __nv_bfloat16* __restrict__ pm, int m_lo_first) {
+                                                        __nv_bfloat16* __restrict__ pm, int m_lo_first,
+                                                        int lo_mode) {
   const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
   const int64_t kpc = (C + 31) / 32 * 32;         // K-major row: 2 * kpc bf16
   const int64_t rp = (C + 7) / 8 * 8;             // MN-major row length
@@ -996,8 +1067,10 @@ __global__ void __launch_bounds__(256) pair_both_kernel(const float* __restrict_
       }
       const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
                                   pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
-      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0]), lo_of(x[1])), pack_bf16(lo_of(x[2]), lo_of(x[3])),
-                                  pack_bf16(lo_of(x[4]), lo_of(x[5])), pack_bf16(lo_of(x[6]), lo_of(x[7])));
+      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0], lo_mode), lo_of(x[1], lo_mode)),
+                                  pack_bf16(lo_of(x[2], lo_mode), lo_of(x[3], lo_mode)),
+                                  pack_bf16(lo_of(x[4], lo_mode), lo_of(x[5], lo_mode)),
+                                  pack_bf16(lo_of(x[6], lo_mode), lo_of(x[7], lo_mode)));
       if (kv && r < R) {
         __nv_bfloat16* o = kv + 64 * (c >> 5) + (c & 31);
         *reinterpret_cast<uint4*>(o) = k_lo_first ? lv : hv;
@@ -1101,7 +1174,7 @@ int workspace(size_t floats, float** out, cudaStream_t st, Workspace* slots = g_
 }
 
 int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both rounded
-int g_scheme = kSchemeTF32BF16;
+int g_scheme = kSchemeBF16X3;
 int g_cta_pair = 1;  // 256 x 256 CTA-pair tiles when the product has more than one row tile
 
 // K splits for the CTA-pair kernel: a product of only a few waves of cluster
@@ -1173,6 +1246,8 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
                 cudaStream_t st) {
   const int64_t kp = (K + 31) / 32 * 32;
   const int64_t mp = (M + 7) / 8 * 8, np_ = (N + 7) / 8 * 8;  // MN-major pair row lengths
+  const bool x3 = g_scheme == kSchemeBF16X3;
+  const int lo_mode = x3 ? 1 : 0;
   // K-major pairs: [M][2kp]; MN-major pairs: [2kp][mp] (bf16, 4 bytes per element pair);
   // a pair the caller computed already (a_pre / b_pre) is used as it is
   const size_t a_bytes = a_pre ? 0 : ((size_t)(TA ? mp : M) * kp * 4 + 1023) / 1024 * 1024;
@@ -1184,18 +1259,18 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
   if (!a_pre) {
     __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>(ws);
     if (TA == 0)
-      pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, w);
+      pair_rows_kernel<<<pair_grid(M), 256, 0, st>>>(A, lda, M, K, kp, 0, lo_mode, w);
     else
-      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(A, lda, K, M, mp, kp, 0, w);
+      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(A, lda, K, M, mp, kp, 0, lo_mode, w);
     TL_TRY(after_launch());
     ap = w;
   }
   if (!b_pre) {
     __nv_bfloat16* w = reinterpret_cast<__nv_bfloat16*>((char*)ws + a_bytes);
     if (TB == 1)
-      pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, w);
+      pair_rows_kernel<<<pair_grid(N), 256, 0, st>>>(B, ldb, N, K, kp, 1, lo_mode, w);
     else
-      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(B, ldb, K, N, np_, kp, 1, w);
+      pair_mn_kernel<<<pair_grid(kp), 256, 0, st>>>(B, ldb, K, N, np_, kp, 1, lo_mode, w);
     TL_TRY(after_launch());
     bp = w;
   }
@@ -1211,6 +1286,7 @@ int launch_pair(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, co
       !(TB ? make_pair_map(&mbp, bp, N, kp, b_box) : make_pair_map_mn(&mbp, bp, np_, kp)))
     return TL_ERR_UNSUPPORTED;
   Params p{(int)M, (int)N, (int)K, C, ldc, bias, accumulate, epilogue, mask, ldm, 1, nullptr};
+  if (x3) return run_tiles<TA, TB, kSchemeBF16X3>(two, ma, map_, mb, mbp, p, M, N, st);
   return run_tiles<TA, TB, kSchemeTF32BF16>(two, ma, map_, mb, mbp, p, M, N, st);
 }
 
@@ -1219,7 +1295,7 @@ int launch(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda, const f
            float* C, int64_t ldc, const float* bias, int accumulate, int epilogue, const float* mask,
            int64_t ldm, const void* a_pre, const void* b_pre, cudaStream_t st) {
   if (!load_encode()) return TL_ERR_UNSUPPORTED;
-  if (g_scheme == kSchemeTF32BF16 && g_split_mode == 0)
+  if ((g_scheme == kSchemeTF32BF16 || g_scheme == kSchemeBF16X3) && g_split_mode == 0)
     return launch_pair<TA, TB>(M, N, K, A, lda, B, ldb, C, ldc, bias, accumulate, epilogue, mask,
                                ldm, a_pre, b_pre, st);
   const int64_t a_rows = TA ? K : M, a_cols = TA ? M : K;
@@ -1301,7 +1377,7 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
 }
 
 bool gemm_uses_pairs(int ta, int tb, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb) {
-  if (g_scheme != kSchemeTF32BF16 || g_split_mode != 0) return false;
+  if ((g_scheme != kSchemeTF32BF16 && g_scheme != kSchemeBF16X3) || g_split_mode != 0) return false;
   if (M < 64 || N < 32 || K < 32 || M > INT32_MAX || N > INT32_MAX || K > INT32_MAX) return false;
   if (lda % 4 || ldb % 4) return false;
   return lda >= (ta ? M : K) && ldb >= (tb ? K : N);
@@ -1320,7 +1396,7 @@ int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* k
   const int64_t cap = 8LL * sm_count();
   pair_both_kernel<<<(unsigned)(r_end < cap ? r_end : cap), 256, 0, st>>>(
       X, ld, rows, cols, reinterpret_cast<__nv_bfloat16*>(kmajor), k_lo_first,
-      reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first);
+      reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first, g_scheme == kSchemeBF16X3 ? 1 : 0);
   return after_launch();
 }
 
@@ -1333,7 +1409,7 @@ int gemm_set_cta_pair(int enable) {
 }
 
 int gemm_set_scheme(int scheme) {
-  if (scheme != kScheme3xTF32 && scheme != kSchemeTF32BF16) return -1;
+  if (scheme != kScheme3xTF32 && scheme != kSchemeTF32BF16 && scheme != kSchemeBF16X3) return -1;
   const int prev = g_scheme;
   g_scheme = scheme;
   return prev;

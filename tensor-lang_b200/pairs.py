@@ -1,7 +1,7 @@
 """GEMM operand pairs, prepared once per operand value.
 
-The TF32+bf16 GEMM scheme needs, besides each fp32 operand, a bf16 pair
-matrix of it (values and lows, see include/tlb200.h); ``tl_gemm`` builds
+The pair GEMM schemes (BF16X3, the default, and TF32+bf16) need a bf16 pair
+matrix of each fp32 operand (values and lows, see include/tlb200.h); ``tl_gemm`` builds
 those with a pre-pass on every call.  In a training iteration one activation
 feeds several products in different roles -- a1 is the K-major A operand of
 the next layer's forward GEMM and the MN-major A operand of that layer's dW;
@@ -14,7 +14,7 @@ hoisted out of the per-iteration graph; the GEMMs then take the prepared
 pairs (``tl_gemm_pairs``).  The pairs are computed exactly as the per-call
 pre-passes would compute them, so results are unchanged.
 
-Only products that take the TF32+bf16 tensor-core path with contiguous
+Only products that take a pair-scheme tensor-core path with contiguous
 operands are planned (``tl_gemm_uses_pairs``); operands sharing a buffer
 through in-place rebinding (updated weights) keep the per-call pre-pass.
 """

@@ -4,11 +4,12 @@ Covers every storage combination the executor uses (A as stored or
 transposed, B as stored or transposed), ragged M/N/K (the tensor-core tiles
 are 128x256x32, so partial tiles exercise TMA zero fill and masked stores;
 K not a multiple of 32 exercises the zero columns of the bf16 pair
-matrices), bias, relu and accumulate, under the default TF32+bf16 operand
-scheme and the three-TF32 scheme, on 256 x 256 CTA-pair tiles (the default
+matrices), bias, relu and accumulate, under the default all-bf16 BF16X3
+operand scheme, the TF32+bf16 scheme and the three-TF32 scheme, on 256 x 256
+CTA-pair tiles (the default
 for more than 128 rows; rows and columns past M and N exercise a pair whose
 second CTA is wholly out of range) and on single-CTA tiles.  Tolerance: rel 1e-4 of max|C| (the GEMM bar);
-the split-TF32 product is expected near 1e-6.  Also checks which path a
+the split products are expected near 1e-6 (split-TF32) to 5e-6 (BF16X3).  Also checks which path a
 shape takes and that no kernel left a device error.
 """
 import ctypes
@@ -66,7 +67,7 @@ def test_gemm_layouts(ta, tb, M, N, K):
     out, ref, path, err = _run(ta, tb, M, N, K)
     assert err == 0
     assert path == 0, "this shape should run on the tensor cores"
-    # split-TF32 keeps fp32-level accuracy: far inside the 1e-4 bar
+    # the split product keeps near-fp32 accuracy: far inside the 1e-4 bar
     assert_close(out, ref, 1e-5, f"gemm ta={ta} tb={tb} {M}x{N}x{K}")
 
 
@@ -117,10 +118,10 @@ def test_gemm_three_tf32_scheme(ta, tb, M, N, K):
         assert_close(out, ref, 1e-5, f"3xTF32 {ta}{tb} {M}x{N}x{K}")
     finally:
         tl.runtime.check(L.tl_gemm_set_scheme(prev.value, None))
-    assert prev.value == 1, "TF32+bf16 is the default scheme"
+    assert prev.value == 2, "BF16X3 is the default scheme"
 
 
-@pytest.mark.parametrize("scheme", [0, 1])
+@pytest.mark.parametrize("scheme", [0, 1, 2])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(300, 520, 200), (1024, 512, 512)])
 def test_gemm_single_cta_tiles(scheme, ta, tb, M, N, K):
@@ -138,6 +139,35 @@ def test_gemm_single_cta_tiles(scheme, ta, tb, M, N, K):
         tl.runtime.check(L.tl_gemm_set_cta_pair(prev_pair.value, None))
         tl.runtime.check(L.tl_gemm_set_scheme(prev_scheme.value, None))
     assert prev_pair.value == 1, "CTA-pair tiles are the default"
+
+
+class _Scheme:
+    """Select a GEMM operand scheme for the duration of a with-block."""
+
+    def __init__(self, scheme):
+        self.scheme = scheme
+
+    def __enter__(self):
+        tl = load_backend()
+        self.L = tl.runtime.lib()
+        self.prev = ctypes.c_int(-1)
+        tl.runtime.check(self.L.tl_gemm_set_scheme(self.scheme, ctypes.byref(self.prev)))
+        return self
+
+    def __exit__(self, *exc):
+        self.L.tl_gemm_set_scheme(self.prev.value, None)
+        return False
+
+
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", SHAPES)
+def test_gemm_tf32_bf16_scheme(ta, tb, M, N, K):
+    """The split-TF32 scheme with bf16 corrections (hi*hi on TF32 plus one
+    bf16 pair MMA) on CTA-pair tiles, split K included, within rel 1e-5."""
+    with _Scheme(1):
+        out, ref, path, err = _run(ta, tb, M, N, K, bias=True)
+    assert err == 0 and path == 0
+    assert_close(out, ref, 1e-5, f"tf32+bf16 {ta}{tb} {M}x{N}x{K}")
 
 
 def test_gemm_scheme_rejects_unknown():
@@ -159,12 +189,18 @@ def test_gemm_explicit_split_mode():
         L.tl_gemm_force_simt(0)
 
 
+@pytest.mark.parametrize("scheme", [1, 2])
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
 @pytest.mark.parametrize("M,N,K", [(300, 520, 200), (1000, 264, 1000)])
-def test_prepared_pairs_match_per_call_pairs(ta, tb, M, N, K):
+def test_prepared_pairs_match_per_call_pairs(scheme, ta, tb, M, N, K):
     """Pairs from tl_gemm_pair_prepare (both layouts from one read, ragged
     shapes: padding rows and columns) give the same product, bit for bit, as
-    the pairs tl_gemm computes itself."""
+    the pairs tl_gemm computes itself, under both pair schemes."""
+    with _Scheme(scheme):
+        _prepared_pairs_case(ta, tb, M, N, K)
+
+
+def _prepared_pairs_case(ta, tb, M, N, K):
     tl = load_backend()
     rt = tl.runtime
     L = rt.lib()
