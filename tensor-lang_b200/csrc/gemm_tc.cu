@@ -64,11 +64,14 @@ __device__ int g_device_error = 0;
 namespace {
 
 constexpr int BM = 128, BN = 256, BK = 32, STAGES = 2;
-// k-blocks per TMEM accumulation chunk (128 deep): each drain reads the whole
+// k-blocks per TMEM accumulation chunk (256 deep): each drain reads the whole
 // accumulator out of tensor memory and slows the MMAs while it runs, so
-// chunks are as long as the accuracy allows (max rel err ~2e-6 at K=65536
-// with 4; one chunk for all of K reaches 2e-4)
-constexpr int KC = 4;
+// chunks are as long as the accuracy allows.  Measured max rel err at
+// K = 4096-65536 (BF16X3): 4.5e-6 with 8, 4.4e-6 with 4; one chunk for all
+// of K reaches 2e-4.  8 is 2.6% faster than 4.
+constexpr int KC = 8;
+// CTA-pair epilogue drains TMEM 16 columns per load (true) or 32 (false)
+constexpr bool kDrain16 = true;
 constexpr int A_TILE = BM * BK * 4;            // 16 KB
 constexpr int B_TILE = BN * BK * 4;            // 32 KB
 constexpr int STAGE_BYTES = 2 * A_TILE + 2 * B_TILE;  // hi + lo of A and B: 96 KB
@@ -174,6 +177,22 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// 16 columns of this warp's 32 TMEM lanes (half the registers of tmem_ld32)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float (&v)[16]) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+      "%12, %13, %14, %15}, [%16];\n\t"
+      "tcgen05.wait::ld.sync.aligned;"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 // Shared-memory matrix descriptor with the tcgen05 version bits.
 //   K-major operands:  128-byte swizzle (16-byte atoms, 8-row period), layout 2
 //   MN-major operands: 128-byte swizzle with 32-byte atoms (4-row period), layout 1
@@ -255,6 +274,7 @@ struct Params {
   int64_t ldm;
   int splits;         // CTA-pair kernel: K split this many ways (1: no split)
   float* partial;     // [splits][M][N] raw sums when splits > 1
+  int tpc = 1;        // CTA-pair kernel: tiles each cluster computes in turn
 };
 
 // Split-K partial of one thread's BN/2 columns of row `row` (no epilogue).
@@ -576,6 +596,25 @@ struct Ring2 {
   static_assert(kBytes * kStages == STAGE2_BYTES * STAGES2, "ring fits the allocation");
 };
 
+// Tile g of a CTA-pair launch, over (split, M tile, N tile) with the N tiles
+// fastest -- consecutive tiles share their A rows in L2 -- and, with split K,
+// all tiles of split 0 first, then split 1, ...; kb0 / nk: the split's k-blocks.
+struct Tile2 {
+  int split, m0, n0, kb0, nk;
+};
+__device__ __forceinline__ Tile2 tile2_of(const Params& p, int g, int m_tiles, int n_tiles,
+                                          int nk_all) {
+  Tile2 t;
+  const int per = m_tiles * n_tiles;
+  t.split = g / per;
+  const int r = g - t.split * per;
+  t.m0 = (r / n_tiles) * 256;
+  t.n0 = (r % n_tiles) * 256;
+  t.kb0 = (int)((int64_t)t.split * nk_all / p.splits);
+  t.nk = (int)((int64_t)(t.split + 1) * nk_all / p.splits) - t.kb0;
+  return t;
+}
+
 __device__ __forceinline__ uint32_t cluster_ctarank() {
   uint32_t r;
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
@@ -660,18 +699,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // clusters walk the N tiles first, so a wave's clusters share A row blocks in
-  // L2; with split K, all tiles of split 0 come first, then split 1, ...
+  // This cluster's tiles: global indices g0 .. g0 + ntl - 1 (tile2_of).
   const int n_tiles = (p.N + 255) / 256, m_tiles = (p.M + 255) / 256;
-  const int cid = (int)(blockIdx.x >> 1);
-  const int split = cid / (m_tiles * n_tiles), tile = cid % (m_tiles * n_tiles);
-  const int m0 = (tile / n_tiles) * 256 + 128 * (int)rank;  // this CTA's rows of A and C
-  const int n0 = (tile % n_tiles) * 256;                    // the tile's columns
-  const int nb = n0 + HB * (int)rank;                              // this CTA's rows of B (N)
   const int nk_all = (p.K + BK - 1) / BK;
-  const int kb0 = (int)((int64_t)split * nk_all / p.splits);       // this split's k-blocks
-  const int nk = (int)((int64_t)(split + 1) * nk_all / p.splits) - kb0;
-  const int nchunks = (nk + KC - 1) / KC;
+  const int cid = (int)(blockIdx.x >> 1);
+  const int g0 = cid * p.tpc;  // this cluster's first tile
+  const int ntl = min(p.tpc, p.splits * m_tiles * n_tiles - g0);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -697,60 +730,74 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   fence_after();
   const uint32_t tmem = *tmem_slot;
 
+  // The stage ring and the two accumulators run on across the cluster's
+  // tiles: k-block `it` (counted over all its tiles) uses stage it % NST,
+  // chunk `cg` accumulator cg & 1, so the loads and MMAs of the next tile
+  // proceed while the epilogue stores the previous one.
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the leader's full[0]
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % NST;
-        const uint32_t ph = (kb / NST) & 1;
-        if (kb >= NST && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) break;
-        unsigned char* st = smem + s * SBYTES;
-        const uint32_t s0 = smem_u32(st);
-        // X3 stage: A pair, B pair; otherwise A, A pair (or lo), B, B pair (or lo)
-        const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
-        const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
-        const uint32_t fb = full0 + 8u * (uint32_t)s;
-        if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * SBYTES);
-        const int k0 = (kb0 + kb) * BK;
-        if (X3) {
-          // no fp32 tiles
-        } else if (TA == 0) {
-          tma_load_2d_pair(sA, &tmA, fb, k0, m0);
-          if (!PAIR) tma_load_2d_pair(sAx, &tmAx, fb, k0, m0);
-        } else {
-#pragma unroll
-          for (int c = 0; c < BM / 32; ++c) {
-            tma_load_2d_pair(sA + c * 4096, &tmA, fb, m0 + 32 * c, k0);
-            if (!PAIR) tma_load_2d_pair(sAx + c * 4096, &tmAx, fb, m0 + 32 * c, k0);
+      bool ok = true;
+      int it = 0;
+      for (int t = 0; t < ntl && ok; ++t) {
+        const Tile2 tt = tile2_of(p, g0 + t, m_tiles, n_tiles, nk_all);
+        const int m0 = tt.m0 + 128 * (int)rank;  // this CTA's rows of A
+        const int nb = tt.n0 + HB * (int)rank;   // this CTA's rows of B (N)
+        for (int kb = 0; kb < tt.nk; ++kb, ++it) {
+          const int s = it % NST;
+          const uint32_t ph = (it / NST) & 1;
+          if (it >= NST && !mbar_wait(smem_u32(&empty[s]), ph ^ 1)) {
+            ok = false;
+            break;
           }
-        }
-        if (X3) {
-          // no fp32 tiles
-        } else if (TB == 1) {
-          tma_load_2d_pair(sB, &tmB, fb, k0, nb);
-          if (!PAIR) tma_load_2d_pair(sBx, &tmBx, fb, k0, nb);
-        } else {
-#pragma unroll
-          for (int c = 0; c < HB / 32; ++c) {
-            tma_load_2d_pair(sB + c * 4096, &tmB, fb, nb + 32 * c, k0);
-            if (!PAIR) tma_load_2d_pair(sBx + c * 4096, &tmBx, fb, nb + 32 * c, k0);
-          }
-        }
-        if (PAIR) {
-          if (TA == 0) {
-            tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
+          unsigned char* st = smem + s * SBYTES;
+          const uint32_t s0 = smem_u32(st);
+          // X3 stage: A pair, B pair; otherwise A, A pair (or lo), B, B pair (or lo)
+          const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
+          const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
+          const uint32_t fb = full0 + 8u * (uint32_t)s;
+          if (leader) mbar_expect_tx(smem_u32(&full[s]), 2 * SBYTES);
+          const int k0 = (tt.kb0 + kb) * BK;
+          if (X3) {
+            // no fp32 tiles
+          } else if (TA == 0) {
+            tma_load_2d_pair(sA, &tmA, fb, k0, m0);
+            if (!PAIR) tma_load_2d_pair(sAx, &tmAx, fb, k0, m0);
           } else {
 #pragma unroll
-            for (int c = 0; c < BM / 64; ++c)
-              tma_load_2d_pair(sAx + c * PAIR_MN_CHUNK, &tmAx, fb, m0 + 64 * c, 2 * k0);
+            for (int c = 0; c < BM / 32; ++c) {
+              tma_load_2d_pair(sA + c * 4096, &tmA, fb, m0 + 32 * c, k0);
+              if (!PAIR) tma_load_2d_pair(sAx + c * 4096, &tmAx, fb, m0 + 32 * c, k0);
+            }
           }
-          if (TB == 1) {
-            tma_load_2d_pair(sBx, &tmBx, fb, 2 * k0, nb);
+          if (X3) {
+            // no fp32 tiles
+          } else if (TB == 1) {
+            tma_load_2d_pair(sB, &tmB, fb, k0, nb);
+            if (!PAIR) tma_load_2d_pair(sBx, &tmBx, fb, k0, nb);
           } else {
 #pragma unroll
-            for (int c = 0; c < HB / 64; ++c)
-              tma_load_2d_pair(sBx + c * PAIR_MN_CHUNK, &tmBx, fb, nb + 64 * c, 2 * k0);
+            for (int c = 0; c < HB / 32; ++c) {
+              tma_load_2d_pair(sB + c * 4096, &tmB, fb, nb + 32 * c, k0);
+              if (!PAIR) tma_load_2d_pair(sBx + c * 4096, &tmBx, fb, nb + 32 * c, k0);
+            }
+          }
+          if (PAIR) {
+            if (TA == 0) {
+              tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
+            } else {
+#pragma unroll
+              for (int c = 0; c < BM / 64; ++c)
+                tma_load_2d_pair(sAx + c * PAIR_MN_CHUNK, &tmAx, fb, m0 + 64 * c, 2 * k0);
+            }
+            if (TB == 1) {
+              tma_load_2d_pair(sBx, &tmBx, fb, 2 * k0, nb);
+            } else {
+#pragma unroll
+              for (int c = 0; c < HB / 64; ++c)
+                tma_load_2d_pair(sBx + c * PAIR_MN_CHUNK, &tmBx, fb, nb + 64 * c, 2 * k0);
+            }
           }
         }
       }
@@ -761,64 +808,72 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = idesc2_tf32<TA, TB ? 0 : 1>();
       bool ok = true;
-      for (int c = 0; c < nchunks && ok; ++c) {
-        const int b = c & 1;
-        const uint32_t acc = tmem + (uint32_t)(b * BN);
-        if (c >= 2 && !mbar_wait(smem_u32(&acc_free[b]), ((c >> 1) - 1) & 1)) break;
-        fence_after();
-        const int kb_end = min(nk, (c + 1) * KC);
-        for (int kb = c * KC; kb < kb_end; ++kb) {
-          const int s = kb % NST;
-          const uint32_t ph = (kb / NST) & 1;
-          if (!mbar_wait(smem_u32(&full[s]), ph)) {
+      int it = 0, cg = 0;
+      for (int t = 0; t < ntl && ok; ++t) {
+        const Tile2 tt = tile2_of(p, g0 + t, m_tiles, n_tiles, nk_all);
+        const int nchunks = (tt.nk + KC - 1) / KC;
+        for (int c = 0; c < nchunks && ok; ++c, ++cg) {
+          const int b = cg & 1;
+          const uint32_t acc = tmem + (uint32_t)(b * BN);
+          if (cg >= 2 && !mbar_wait(smem_u32(&acc_free[b]), ((cg >> 1) - 1) & 1)) {
             ok = false;
             break;
           }
           fence_after();
-          unsigned char* st = smem + s * SBYTES;
-          const uint32_t s0 = smem_u32(st);
-          const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
-          const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
-          if constexpr (X3) {
-            // values x values: the A pair's first half (k-steps 0, 1) with
-            // the B pair's second half (k-steps 2, 3; B pairs hold lows first)
-#pragma unroll
-            for (int k = 0; k < 2; ++k) {
-              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
-              mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
-                        TB ? kmajor_desc(sBx, k + 2) : mn16_desc(sBx, k + 2),
-                        idesc2_bf16<TA, TB ? 0 : 1>(), first);
+          const int kb_end = min(tt.nk, (c + 1) * KC);
+          for (int kb = c * KC; kb < kb_end; ++kb, ++it) {
+            const int s = it % NST;
+            const uint32_t ph = (it / NST) & 1;
+            if (!mbar_wait(smem_u32(&full[s]), ph)) {
+              ok = false;
+              break;
             }
-          } else if constexpr (PAIR) {
+            fence_after();
+            unsigned char* st = smem + s * SBYTES;
+            const uint32_t s0 = smem_u32(st);
+            const uint32_t sA = s0, sAx = X3 ? s0 : s0 + A_TILE;
+            const uint32_t sB = sAx + A_TILE, sBx = X3 ? s0 + A_TILE : sB + B_HALF;
+            if constexpr (X3) {
+              // values x values: the A pair's first half (k-steps 0, 1) with
+              // the B pair's second half (k-steps 2, 3; B pairs hold lows first)
 #pragma unroll
-            for (int k = 0; k < BK / 8; ++k) {
-              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
-              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
-              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
-              mma2_tf32(acc, a, bh, idesc, first);
+              for (int k = 0; k < 2; ++k) {
+                const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+                mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
+                          TB ? kmajor_desc(sBx, k + 2) : mn16_desc(sBx, k + 2),
+                          idesc2_bf16<TA, TB ? 0 : 1>(), first);
+              }
+            } else if constexpr (PAIR) {
+#pragma unroll
+              for (int k = 0; k < BK / 8; ++k) {
+                const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+                const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+                const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+                mma2_tf32(acc, a, bh, idesc, first);
+              }
             }
+            if constexpr (PAIR) {
+#pragma unroll
+              for (int k = 0; k < 4; ++k)
+                mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
+                          TB ? kmajor_desc(sBx, k) : mn16_desc(sBx, k), idesc2_bf16<TA, TB ? 0 : 1>());
+            } else {
+#pragma unroll
+              for (int k = 0; k < BK / 8; ++k) {
+                const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
+                const uint64_t al = TA ? mnmajor_desc(sAx, k) : kmajor_desc(sAx, k);
+                const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
+                const uint64_t bl = TB ? kmajor_desc(sBx, k) : mnmajor_desc(sBx, k);
+                const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
+                mma2_tf32(acc, a, bh, idesc, first);
+                mma2_tf32(acc, a, bl, idesc, 1u);
+                mma2_tf32(acc, al, bh, idesc, 1u);
+              }
+            }
+            mma2_commit_both(smem_u32(&empty[s]));  // frees stage s in both CTAs
           }
-          if constexpr (PAIR) {
-#pragma unroll
-            for (int k = 0; k < 4; ++k)
-              mma2_bf16(acc, TA ? mn16_desc(sAx, k) : kmajor_desc(sAx, k),
-                        TB ? kmajor_desc(sBx, k) : mn16_desc(sBx, k), idesc2_bf16<TA, TB ? 0 : 1>());
-          } else {
-#pragma unroll
-            for (int k = 0; k < BK / 8; ++k) {
-              const uint64_t a = TA ? mnmajor_desc(sA, k) : kmajor_desc(sA, k);
-              const uint64_t al = TA ? mnmajor_desc(sAx, k) : kmajor_desc(sAx, k);
-              const uint64_t bh = TB ? kmajor_desc(sB, k) : mnmajor_desc(sB, k);
-              const uint64_t bl = TB ? kmajor_desc(sBx, k) : mnmajor_desc(sBx, k);
-              const uint32_t first = (kb == c * KC && k == 0) ? 0u : 1u;
-              mma2_tf32(acc, a, bh, idesc, first);
-              mma2_tf32(acc, a, bl, idesc, 1u);
-              mma2_tf32(acc, al, bh, idesc, 1u);
-            }
-          }
-          mma2_commit_both(smem_u32(&empty[s]));  // frees stage s in both CTAs
+          mma2_commit_both(smem_u32(&acc_full[b]));  // chunk ready in both CTAs
         }
-        mma2_commit_both(smem_u32(&acc_full[b]));  // chunk ready in both CTAs
       }
     }
     __syncwarp();
@@ -827,38 +882,56 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const int e = warp - 2;
     const int quarter = warp & 3;
     const int half = e >= 4 ? 1 : 0;
-    const int row = m0 + quarter * 32 + lane;
     const uint32_t lane_base = (uint32_t)(quarter * 32) << 16;
     const uint32_t free0 = mapa_shared(smem_u32(&acc_free[0]), 0);  // the leader's acc_free[0]
+    const uint32_t tbase = tmem + lane_base + (uint32_t)(half * (BN / 2));
     float sum[BN / 2];
-#pragma unroll
-    for (int j = 0; j < BN / 2; ++j) sum[j] = 0.f;
     bool ok = true;
-    for (int c = 0; c < nchunks; ++c) {
-      const int b = c & 1;
-      if (!mbar_wait(smem_u32(&acc_full[b]), (c >> 1) & 1)) {
-        ok = false;
-        break;
-      }
-      fence_after();
-      __syncwarp();
-      const uint32_t base = tmem + lane_base + (uint32_t)(b * BN + half * (BN / 2));
+    int cg = 0;
+    for (int g = g0; g < g0 + ntl && ok; ++g) {
+      // only the chunk count is needed while the tile drains (the registers
+      // hold the row's partial sums); its position is derived for the store
+      const int nchunks = (tile2_of(p, g, m_tiles, n_tiles, nk_all).nk + KC - 1) / KC;
 #pragma unroll
-      for (int q = 0; q < BN / 64; ++q) {
-        float v[32];
-        tmem_ld32(base + q * 32, v);
+      for (int j = 0; j < BN / 2; ++j) sum[j] = 0.f;
+      for (int c = 0; c < nchunks; ++c, ++cg) {
+        const int b = cg & 1;
+        if (!mbar_wait(smem_u32(&acc_full[b]), (cg >> 1) & 1)) {
+          ok = false;
+          break;
+        }
+        fence_after();
+        __syncwarp();
+        const uint32_t base = tbase + (uint32_t)(b * BN);
+        if constexpr (kDrain16) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) sum[q * 32 + j] = __fadd_rn(sum[q * 32 + j], v[j]);
+          for (int q = 0; q < BN / 32; ++q) {
+            float v[16];
+            tmem_ld16(base + q * 16, v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) sum[q * 16 + j] = __fadd_rn(sum[q * 16 + j], v[j]);
+          }
+        } else {
+#pragma unroll
+          for (int q = 0; q < BN / 64; ++q) {
+            float v[32];
+            tmem_ld32(base + q * 32, v);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) sum[q * 32 + j] = __fadd_rn(sum[q * 32 + j], v[j]);
+          }
+        }
+        fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
       }
-      fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
-    }
-    if (ok) {
-      if (p.splits > 1)
-        store_partial(p, split, row, n0 + half * (BN / 2), sum);
-      else
-        store_row(p, row, n0 + half * (BN / 2), sum);
+      if (ok) {
+        const Tile2 tt = tile2_of(p, g, m_tiles, n_tiles, nk_all);
+        const int row = tt.m0 + 128 * (int)rank + quarter * 32 + lane;
+        if (p.splits > 1)
+          store_partial(p, tt.split, row, tt.n0 + half * (BN / 2), sum);
+        else
+          store_row(p, row, tt.n0 + half * (BN / 2), sum);
+      }
     }
   }
   fence_before();
@@ -1176,6 +1249,29 @@ int workspace(size_t floats, float** out, cudaStream_t st, Workspace* slots = g_
 int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both rounded
 int g_scheme = kSchemeBF16X3;
 int g_cta_pair = 1;  // 256 x 256 CTA-pair tiles when the product has more than one row tile
+int g_tiles_per_cluster = 4;  // upper bound on the tiles one CTA pair computes in turn
+
+// Tiles per cluster for a CTA-pair launch of `tiles` tiles: each cluster
+// launch pays a prologue (barrier set-up, TMEM allocation, pipeline fill) and
+// an exposed epilogue (the tile store); a cluster that computes several
+// tiles in turn overlaps both with the MMAs of its next tile.  Used only
+// while the launch keeps at least four waves of clusters (so the hardware
+// scheduler still balances them) and its last wave is no emptier than with
+// one tile per cluster (wave efficiency within 1%).
+int tiles_per_cluster(int64_t tiles) {
+  const int64_t slots = sm_count() / 2;
+  if (slots < 1) return 1;
+  auto eff = [&](int64_t clusters) {
+    const int64_t waves = (clusters + slots - 1) / slots;
+    return (double)clusters / (double)(waves * slots);
+  };
+  const double base = eff(tiles);
+  for (int t = g_tiles_per_cluster; t >= 2; --t) {
+    const int64_t clusters = (tiles + t - 1) / t;
+    if (clusters >= 4 * slots && eff(clusters) >= base - 0.01) return t;
+  }
+  return 1;
+}
 
 // K splits for the CTA-pair kernel: a product of only a few waves of cluster
 // tiles leaves most SM pairs idle in its last wave (e.g. 256 tiles on 74
@@ -1206,12 +1302,14 @@ int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CU
     if (2 * clusters * splits > INT32_MAX) return TL_ERR_UNSUPPORTED;
     Params q = p;
     q.splits = splits;
+    q.tpc = tiles_per_cluster(clusters * splits);
+    const int64_t launched = (clusters * splits + q.tpc - 1) / q.tpc;  // clusters launched
     if (splits > 1) {
       float* part = nullptr;
       TL_TRY(workspace((size_t)splits * M * N, &part, st, g_ws_partial));
       q.partial = part;
     }
-    kern<<<(unsigned)(2 * clusters * splits), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, q);
+    kern<<<(unsigned)(2 * launched), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, q);
     if (splits > 1) {
       TL_TRY(after_launch());
       const int64_t units = (N % 4 == 0) ? M * N / 4 : M * N;

@@ -170,6 +170,17 @@ def test_gemm_tf32_bf16_scheme(ta, tb, M, N, K):
     assert_close(out, ref, 1e-5, f"tf32+bf16 {ta}{tb} {M}x{N}x{K}")
 
 
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+def test_gemm_several_tiles_per_cluster(ta, tb):
+    """A launch of many waves (74 x 16 CTA-pair tiles, ragged M, N and K on
+    a 148-SM B200): each CTA pair computes two or more tiles in turn, the
+    stage ring and accumulators running on across them."""
+    M, N, K = 18900, 4056, 520
+    out, ref, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
+    assert err == 0 and path == 0
+    assert_close(out, ref, 1e-5, f"tiles per cluster {ta}{tb} {M}x{N}x{K}")
+
+
 def test_gemm_scheme_rejects_unknown():
     tl = load_backend()
     L = tl.runtime.lib()
