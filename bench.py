@@ -52,7 +52,8 @@ GEMM_SCHEMES = {
 # DRAM bytes (read + written) of one hidden-layer GEMM kernel launch
 # (65536 x 4096 x 4096, CTA pairs) per scheme, from a one-pass ncu capture of
 # `bench.py --micro gemm --gemm-m 65536`; None where not captured
-GEMM_TRAFFIC_BYTES = {"tf32bf16": 10_070_651_136 + 1_101_682_176}
+GEMM_TRAFFIC_BYTES = {"bf16x3": 5_250_906_112 + 1_057_456_640,
+                      "tf32bf16": 10_070_651_136 + 1_101_682_176}
 
 
 def set_gemm_scheme(tl, name):
@@ -304,7 +305,9 @@ def run_ours(args, rank, world, local):
     # first iteration eagerly (counts kernel launches), then capture the graph
     rt.launch_count(reset=True)
     loop.run_eager()
-    launches_per_step = rt.launch_count()
+    n_eager = rt.launch_count(reset=True)
+    loop.run_hoisted()  # hoisted steps run outside the per-iteration graph
+    launches_per_step = n_eager - rt.launch_count()
     loop.capture()
     for _ in range(args.warmup):
         loop.replay(1)
