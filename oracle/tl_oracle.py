@@ -198,8 +198,12 @@ def _argfirst(x, axis, largest):
     return (np.argmax(x, axis=axis) if largest else np.argmin(x, axis=axis))
 
 
-def op_forward(expr: dict, vals: Dict[str, np.ndarray], dt=np.float64) -> np.ndarray:
-    """Evaluate one ``let`` expression; ``vals`` maps operand names to arrays."""
+def op_forward(expr: dict, vals: Dict[str, np.ndarray], dt=np.float64,
+               numpy_broadcast: bool = False) -> np.ndarray:
+    """Evaluate one ``let`` expression; ``vals`` maps operand names to arrays.
+
+    ``numpy_broadcast``: a square 2-D op 1-D reads ``B[j]`` (NumPy) instead
+    of the reference's ``B[i]``."""
     t = expr["type"]
     T = np.dtype(dt).type
     if t in _BIN:
@@ -208,7 +212,8 @@ def op_forward(expr: dict, vals: Dict[str, np.ndarray], dt=np.float64) -> np.nda
         if a.shape == b.shape:  # elementwise, kernel_generator.py:246-275
             return op(a, b).astype(dt)
         if a.ndim == 2 and b.ndim == 1:  # binary_broadcast :281-348
-            if a.shape[0] == b.shape[0]:
+            square = numpy_broadcast and a.shape[1] == b.shape[0]
+            if a.shape[0] == b.shape[0] and not square:
                 return op(a, b[:, None]).astype(dt)  # B[i]
             return op(a, b[None, :]).astype(dt)  # B[j]
         if a.ndim == 1 and b.ndim == 1 and b.shape[0] == 1:  # binary_1d_broadcast :354-377
@@ -359,8 +364,11 @@ def unbroadcast(g: np.ndarray, shape: tuple) -> np.ndarray:
 
 
 class _Graph:
-    def __init__(self, dt):
+    def __init__(self, dt, textbook_ce=False):
         self.dt = dt
+        # cross_entropy through a row softmax (its only consumer, 2-D, axis 1):
+        # the textbook (p - t) / B for the logits, nothing for p
+        self.textbook_ce = textbook_ce
         self.nodes: List[_Node] = []
         self.tensors: Dict[str, np.ndarray] = {}
         self.requires: set = set()
@@ -395,6 +403,10 @@ class _Graph:
         for n in need:
             if n in self.tensors:
                 self.grads[n] = np.zeros_like(self.tensors[n])
+        self._consumers: Dict[str, int] = {}
+        for n in self.nodes:
+            for i in n.ins:
+                self._consumers[i] = self._consumers.get(i, 0) + 1
         self.grads[loss] = np.ones_like(self.tensors[loss])
         for node in reversed(self.nodes):
             if node.out not in self.grads:
@@ -492,6 +504,11 @@ class _Graph:
                 c = np.clip(q.astype(np.int64), 0, p.shape[1] - 1)
                 q = np.eye(p.shape[1], dtype=V)[c]
             sg = g.item() if g.size == 1 else g
+            sm = next((n for n in self.nodes if n.out == ins[0] and n.op == "softmax"), None)
+            if (self.textbook_ce and sm is not None and p.ndim == 2 and
+                    sm.meta.get("axis") in (1, -1) and self._consumers.get(ins[0]) == 1):
+                self._acc(sm.ins[0], (p - q) / p.shape[0] * sg)
+                return
             self._acc(ins[0], (p - q) / p.shape[0] * sg)
 
 
@@ -527,14 +544,17 @@ class OracleProgram:
     """
 
     def __init__(self, ast, env, dtype=np.float64, feeds=None, load_files=None,
-                 record="extended"):
+                 record="extended", semantics="reference"):
         self.ast = ast
         self.env = {k: _shape(v["shape"]) for k, v in env.items()}
         self.dt = np.dtype(dtype).type
         self.feeds = {k: np.asarray(v) for k, v in (feeds or {}).items()}
         self.load_files = load_files or {}
         self.recorded_ops = _RECORDED_EXTENDED if record == "extended" else _RECORDED_REFERENCE
-        self.graph = _Graph(self.dt)
+        if semantics not in ("reference", "numpy"):
+            raise ValueError(f"semantics must be 'reference' or 'numpy', not {semantics!r}")
+        self.numpy_broadcast = semantics == "numpy"
+        self.graph = _Graph(self.dt, textbook_ce=semantics == "numpy")
         self.requires: set = set()
         self.tensors: Dict[str, np.ndarray] = {}
         self.outputs: Dict[str, np.ndarray] = {}
@@ -606,7 +626,7 @@ class OracleProgram:
         if name in self.feeds and node["expr"]["type"] in ("fill",):
             self.tensors[name] = self.feeds[name].astype(self.dt)
             return
-        self.tensors[name] = op_forward(node["expr"], self.tensors, self.dt)
+        self.tensors[name] = op_forward(node["expr"], self.tensors, self.dt, self.numpy_broadcast)
 
     def _register_all(self):
         for k, v in self.tensors.items():

@@ -49,8 +49,12 @@ def grad_name(n: str) -> str:
 
 class BackwardPlanner:
     def __init__(self, nodes: List[Node], requires: set, shapes: Dict[str, Shape],
-                 prefix: str = "bw", divisors: Optional[Dict[str, float]] = None):
+                 prefix: str = "bw", divisors: Optional[Dict[str, float]] = None,
+                 textbook_ce: bool = False):
         self.nodes = nodes
+        # cross_entropy through a row softmax: the textbook (p - t) / B for the
+        # logits instead of the reference's chained softmax VJP
+        self.textbook_ce = textbook_ce
         self.requires = set(requires)
         self.shapes = shapes
         self.prefix = prefix
@@ -366,6 +370,19 @@ class BackwardPlanner:
         ps, ts = tuple(S[p]), tuple(S[tgt])
         onehot = 1 if ts == ps else 0
         B = self.divisors.get(("ce", node.out), float(ps[0]))
+        if p in fused_softmax and self.textbook_ce:
+            # d loss / d z = (p - t) / B * g, in the order of the literal VJP's
+            # minus, div, mult; p itself gets nothing from this path
+            z = next(n for n in active if n.out == p and n.op == "softmax").ins[0]
+            if z not in self.requires:
+                return
+            if not onehot:
+                raise NotImplementedError("the textbook cross_entropy gradient takes one-hot targets")
+            d = self._ew(ps, "minus", [self._val(p, "full"), self._val(tgt, "full")])
+            d2 = self._ew(ps, "div", [self._val(d, "full"), ("const", float(B))])
+            d3 = self._ew(ps, "mult", [self._val(d2, "full"), self._val(g, "scalar")])
+            self._accumulate_value(z, d3, ps)
+            return
         if p in fused_softmax:
             sm = next(n for n in active if n.out == p and n.op == "softmax")
             z = sm.ins[0]

@@ -214,6 +214,14 @@ class Program:
     named tensors; ``fetch`` names the tensors the caller will read (None =
     every named tensor, like the reference's cache of every result); anything
     else may be fused away.
+
+    ``semantics="reference"`` (default) keeps the reference's literal rules;
+    ``"numpy"`` switches two of them to the textbook ones: a square 2-D op
+    1-D broadcast reads ``B[j]`` as NumPy does (the reference reads ``B[i]``
+    whenever the row counts match, kernel_generator.py:303-348), and the
+    gradient of cross_entropy through a row softmax is ``(p - t) / B``
+    (the reference chains the softmax VJP after cross_entropy's,
+    autograd.py:563-580, 691-704).  One-hot targets only in that mode.
     """
 
     def __init__(self, ast: list, env: Optional[dict] = None, *, device: int = 0,
@@ -221,7 +229,10 @@ class Program:
                  load_files: Optional[Dict[str, np.ndarray]] = None, record: str = "extended",
                  use_graphs: bool = True, fuse_ops: bool = True, save_dir: Optional[str] = None,
                  shapes: Optional[Dict[str, Shape]] = None, divisors: Optional[dict] = None,
-                 grad_hook=None):
+                 grad_hook=None, semantics: str = "reference"):
+        if semantics not in ("reference", "numpy"):
+            raise ValueError(f"semantics must be 'reference' or 'numpy', not {semantics!r}")
+        self.semantics = semantics
         self.ast = ast
         self.device_index = int(device)
         self.shapes: Dict[str, Shape] = dict(shapes) if shapes else complete_env(ast, env or {})
@@ -235,7 +246,7 @@ class Program:
         self.divisors = divisors or {}
         self.grad_hook = grad_hook  # (program, exposed grads, backward steps) -> backward steps
         self.arena_names: List[str] = []  # allocated contiguously (one all-reduce span)
-        self.gen = KernelGenerator(False)
+        self.gen = KernelGenerator(False, numpy_broadcast=semantics == "numpy")
         self.nodes: List[Node] = []
         self.requires: set = set()
         self.kinfos: List[tuple] = []
@@ -353,7 +364,8 @@ class Program:
             for node in ast:
                 if node["type"] == "backward":
                     planner = BackwardPlanner(self.nodes, self.requires, self.shapes,
-                                              prefix=f"tb{nbw}_", divisors=self.divisors)
+                                              prefix=f"tb{nbw}_", divisors=self.divisors,
+                                              textbook_ce=self.semantics == "numpy")
                     nbw += 1
                     steps, exposed = planner.plan(node["loss_tensor"])
                     self.phase_bw += steps
@@ -369,7 +381,8 @@ class Program:
         bw_steps: List[Step] = []
         if bw is not None:
             planner = BackwardPlanner(self.nodes, self.requires, self.shapes, prefix=f"{label}b_",
-                                      divisors=self.divisors)
+                                      divisors=self.divisors,
+                                      textbook_ce=self.semantics == "numpy")
             bw_steps, exposed = planner.plan(body[bw]["loss_tensor"])
             self.exposed_grads = sorted(set(self.exposed_grads) | set(exposed))
             if self.grad_hook is not None:

@@ -19,7 +19,9 @@ Differences, all additions:
   ``('cross_entropy_onehot', ...)``;
 * ``argmax``/``argmin`` accept axis 0 (``'argmax_axis0'``, ``'argmin_axis0'``)
   and ``argmin`` the full tensor (``'argmin_full'``);
-* shapes the reference returns ``None`` for raise ``NotImplementedError``.
+* shapes the reference returns ``None`` for raise ``NotImplementedError``;
+* ``numpy_broadcast=True`` (the backend's ``semantics="numpy"``) gives a
+  square 2-D op 1-D the NumPy kernel (``B[j]``) instead of the per-row one.
 """
 from __future__ import annotations
 
@@ -48,8 +50,9 @@ def _prod(shape) -> int:
 class KernelGenerator:
     """Per-op lowering with the reference's signatures (kernel_generator.py:9-2132)."""
 
-    def __init__(self, DEBUG_MODE=False):
+    def __init__(self, DEBUG_MODE=False, numpy_broadcast=False):
         self.DEBUG_MODE = DEBUG_MODE
+        self.numpy_broadcast = numpy_broadcast
 
     def _validate(self, kernel_type, op_type):
         """kernel_generator.py:21-146: unknown kernel types / ops raise ValueError."""
@@ -72,7 +75,10 @@ class KernelGenerator:
     def binary_broadcast(self, op_name, op_type, name, arg1, arg2, shape1, shape2, output_shape):
         self._validate("binary_broadcast", op_type)
         rows, cols = output_shape
-        if shape1[0] == shape2[0]:
+        # the reference's rule (:303-348): B[i] whenever the row counts match;
+        # NumPy's reads B[j] when the columns match too (square inputs)
+        square = self.numpy_broadcast and shape1[1] == shape2[0]
+        if shape1[0] == shape2[0] and not square:
             return "", (f"{op_type}_broadcast_rows", name, arg1, arg2, rows, cols)
         return "", (f"{op_type}_broadcast", name, arg1, arg2, rows, cols)
 

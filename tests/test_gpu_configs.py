@@ -106,3 +106,27 @@ def test_mlp3_graph_replay_matches_eager():
     b = tl.Program(ast, None, feeds=feeds, fetch=fetch, use_graphs=False).run()
     for k in fetch:
         np.testing.assert_array_equal(a[k], b[k], err_msg=k)
+
+
+def test_numpy_semantics_match_the_oracle():
+    """semantics="numpy": the square broadcast reads B[j] and the softmax ->
+    cross_entropy gradient is (p - t) / B, on the GPU as in the oracle."""
+    tl = load_backend()
+    pr = tl.programs
+    N = 1000
+    ast, feeds = pr.fused_chain(N), pr.fused_chain_inputs(N, seed=5)
+    P = tl.Program(ast, None, feeds=feeds, fetch=["y", "m"], semantics="numpy")
+    out = P.run()
+    ref = OracleProgram(ast, _env(P), dtype=np.float64, feeds=feeds, semantics="numpy").run()
+    ref32 = OracleProgram(ast, _env(P), dtype=np.float32, feeds=feeds, semantics="numpy").run()
+    P.free()
+    assert_close(out["y"], ref["y"], 1e-5, "y")
+    np.testing.assert_array_equal(out["m"], ref32["m"])
+    ast, feeds = pr.mlp2_step(), pr.mlp2_inputs(seed=2)
+    P = tl.Program(ast, None, feeds=feeds, semantics="numpy")
+    out = P.run()
+    ref = OracleProgram(ast, _env(P), dtype=np.float64, feeds=feeds, semantics="numpy").run()
+    P.free()
+    for k in ["loss", "z_grad", "p_grad", "W1_grad", "b1_grad", "W2_grad", "b2_grad",
+              "W1_new", "b2_new"]:
+        assert_close(out[k], ref[k], 1e-4, k)
