@@ -383,7 +383,8 @@ def run_ours(args, rank, world, local):
             "roofline": {"bound": "tensor", "kernel": f"GEMM {M}x{N}x{K} ({path})",
                          "achieved": tflops, "peak": bf16, "unit": "TFLOP/s",
                          "frac": tflops / bf16, "peak_source": f"{src} bf16 dense (burst)",
-                         "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_scheme),
+                         # captured for the one-GPU launch (65536 rows) only
+                         "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_scheme) if M == B_GLOBAL else None,
                          "scheme_ceiling": ceiling,
                          "frac_of_scheme_ceiling": tflops / ceiling},
             "e2e": {"value": 1000.0 / max(all_e2e), "unit": "steps/s",
