@@ -572,8 +572,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 // m0+128r..+127 of A and rows n0+128r..+127 of B (the N axis) for every
 // k-block into its own shared memory; the leader (rank 0) issues the MMAs,
 // which read both CTAs' tiles and accumulate 128 x 256 in each CTA's tensor
-// memory.  Per CTA a k-block moves 64 KB instead of the single-CTA tile's
-// 96 KB for the same MMA work, and three stages fit.
+// memory.  Per CTA a k-block moves 64 KB under TF32+bf16 (three stages fit)
+// instead of the single-CTA tile's 96 KB for the same MMA work, and 32 KB
+// under BF16X3 (six stages).  On launches of many waves a cluster computes up
+// to four tiles in turn (Params.tpc), its ring and accumulators running on
+// across them, so one tile's store overlaps the next tile's MMAs.
 //
 // Barriers: every TMA load of both CTAs completes on the leader's full[s]
 // (the .cta_group::2 form of the load may signal the peer CTA's barrier);
