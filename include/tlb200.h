@@ -271,6 +271,12 @@ int  tl_gemm_uses_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t 
 int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                   const float* A, int64_t lda, const float* B, int64_t ldb,
                   const float* C, int64_t ldc);
+/* The tensor-core launch for an M x N x K product (no reference
+ * counterpart; host-only, no GPU needed): plan[0] 1 for 256 x 256 CTA-pair
+ * tiles, 0 for 128 x 256 single-CTA tiles; plan[1] K splits; plan[2] tiles
+ * each CTA pair computes in turn; plan[3] clusters (CTA pairs) or CTAs
+ * launched.  Uses this device's SM count (148 when no GPU is visible). */
+int  tl_gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* plan);
 /* Path selection: 0 automatic (tensor cores when the shape allows, the raw
  * operand as the TF32 "hi" part); 1 force the CUDA-core path; 2 automatic,
  * with hi and lo both rounded to TF32 explicitly in the pre-pass. */

@@ -19,6 +19,7 @@ int gemm_tc(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int
             int epilogue, const float* mask, int64_t ldm, const void* a_pair, const void* b_pair,
             cudaStream_t st);
 bool gemm_uses_pairs(int ta, int tb, int64_t M, int64_t N, int64_t K, int64_t lda, int64_t ldb);
+int gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* out);
 int64_t pair_bytes(int64_t rows, int64_t cols, int layout);
 int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
                  int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st);
@@ -220,6 +221,10 @@ int tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, cons
   if (!tl::g_force_simt && tl::gemm_tc_ok(trans_a, trans_b, M, N, K, A, lda, B, ldb, C, ldc))
     return 0;
   return 1;
+}
+
+int tl_gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* plan) {
+  return tl::gemm_tc_plan(M, N, K, plan);
 }
 
 int tl_gemm_force_simt(int force) {

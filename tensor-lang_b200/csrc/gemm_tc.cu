@@ -1501,6 +1501,29 @@ int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* k
   return after_launch();
 }
 
+// The launch run_tiles makes for an M x N x K product on the tensor cores
+// (host-side: the same split_count and tiles_per_cluster decisions).
+int gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* out) {
+  if (M <= 0 || N <= 0 || K <= 0 || !out) return TL_ERR_INVALID_ARG;
+  const bool two = g_cta_pair && M > BM;
+  if (!two) {
+    out[0] = 0;
+    out[1] = 1;
+    out[2] = 1;
+    out[3] = (int)(((N + BN - 1) / BN) * ((M + BM - 1) / BM));
+    return TL_OK;
+  }
+  const int64_t clusters = ((M + 255) / 256) * ((N + 255) / 256);
+  const int splits = split_count(clusters, (K + BK - 1) / BK);
+  if (2 * clusters * splits > INT32_MAX) return TL_ERR_UNSUPPORTED;
+  const int tpc = tiles_per_cluster(clusters * splits);
+  out[0] = 1;
+  out[1] = splits;
+  out[2] = tpc;
+  out[3] = (int)((clusters * splits + tpc - 1) / tpc);
+  return TL_OK;
+}
+
 void gemm_set_split_mode(int mode) { g_split_mode = mode; }
 
 int gemm_set_cta_pair(int enable) {

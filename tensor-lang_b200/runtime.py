@@ -111,6 +111,7 @@ _SIGS = [
                               c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_int64, c_void_p,
                               c_int, c_int, c_void_p, c_int64, c_void_p]),
     ("tl_gemm_pair_bytes", c_int64, [c_int64, c_int64, c_int]),
+    ("tl_gemm_tc_plan", c_int, [c_int64, c_int64, c_int64, ctypes.POINTER(c_int)]),
     ("tl_gemm_pair_prepare", c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
                                      c_void_p, c_int, c_void_p]),
     ("tl_gemm_uses_pairs", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_int64, c_int64]),
