@@ -347,6 +347,9 @@ def run_ours(args, rank, world, local):
     on_tc = L.tl_gemm_path(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("a2"), N) == 0
     path = (f"{GEMM_SCHEMES[args.gemm_scheme][1]}, CTA-pair 256x256 tiles"
             if on_tc else "CUDA-core fp32")
+    plan = (ctypes.c_int * 4)()
+    rt.check(L.tl_gemm_tc_plan(M, N, K, plan), "gemm plan")
+    gemm_plan = {"k_splits": plan[1], "tiles_per_cluster": plan[2], "clusters": plan[3]}
     loss = float(P.read("loss").reshape(-1)[0])
 
     fused = None
@@ -386,7 +389,8 @@ def run_ours(args, rank, world, local):
                          # captured for the one-GPU launch (65536 rows) only
                          "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_scheme) if M == B_GLOBAL else None,
                          "scheme_ceiling": ceiling,
-                         "frac_of_scheme_ceiling": tflops / ceiling},
+                         "frac_of_scheme_ceiling": tflops / ceiling,
+                         "launch": gemm_plan},
             "e2e": {"value": 1000.0 / max(all_e2e), "unit": "steps/s",
                     "h2d_bytes_per_step": int(xs.nbytes + ts.nbytes) * world,
                     "d2h_bytes_per_step": 4 * world},
