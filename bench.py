@@ -246,8 +246,8 @@ def e2e_time(tl, dev, loop, stream, px, pt, pl, xs, ts, steps):
     try:
         run(2)  # untimed: warms the copy path
         return run(steps)
-    finally:
-        rt.check(L.tl_stream_sync(copy), "sync copy")
+    finally:  # cleanup: an error raised above is the one to report
+        L.tl_stream_sync(copy)
         L.tl_stream_destroy(copy)
         hx.free()
         ht.free()
