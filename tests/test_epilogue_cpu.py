@@ -114,3 +114,24 @@ def test_operand_pairs_planned_once_per_value():
                      s.args[10][1] if s.args[10][0] == "ptr" else None):
             assert name is None or name.startswith("__pair_")
     assert not any("W2" in w for s in prep.values() for w in s.writes)
+
+
+def test_no_operand_pairs_under_the_three_tf32_scheme():
+    """The three-TF32 scheme reads no pair matrices, so nothing is planned."""
+    import ctypes
+    tl = load_backend()
+    L = tl.runtime.lib()
+    prev = ctypes.c_int(-1)
+    assert L.tl_gemm_set_scheme(0, ctypes.byref(prev)) == 0
+    try:
+        pr = tl.programs
+        kw = dict(B=4096, I=1024, H=4096, C=10)
+        P = tl.Program(pr.mlp3_train(epochs=2, **kw), None, fetch=["loss", "W3"])
+        P._fuse_all()
+        loop = P.loops[0]
+        assert not loop.hoisted
+        names = [getattr(s, "fname", "") for s in loop.body()]
+        assert "tl_gemm_pair_prepare" not in names and "tl_gemm_pairs" not in names
+    finally:
+        L.tl_gemm_set_scheme(prev.value, None)
+    assert prev.value == 2  # BF16X3 is the default
