@@ -134,12 +134,14 @@ int  tl_reduce_cols(int op, const float* in, float* out, int64_t rows, int64_t c
  * every device allocation, or a fixed-budget path that must not allocate
  * while it runs).  Its scratch is a 1 MiB file-scope device array of the
  * library, held by every GPU that loads the library until the process exits.
- * cols may be at most 65280 for argmax/argmin and 130560 for the other ops
- * ((1 MiB - 4 KiB) / 16 or / 8 bytes of partials per column); larger sizes
- * return TL_ERR_INVALID_ARG without launching anything.  The first call on a device
- * looks up the array's device address (cudaGetSymbolAddress) and should come
- * before any stream capture.  All calls share the array: calls whose kernels
- * overlap on the GPU race, so issue them in one stream order. */
+ * cols may be at most 64512 for argmax/argmin and 129024 for the other ops
+ * ((1 MiB - 16 KiB of completion counters) / 16 or / 8 bytes of partials per
+ * column), whatever the alignment of `in` or the remainder of cols / 4;
+ * larger sizes return TL_ERR_INVALID_ARG without launching anything.  Each
+ * call looks up the array's device address (cudaGetSymbolAddress) on the
+ * current device; the first call on a device also loads the module there and
+ * should come before any stream capture.  All calls share the array: calls
+ * whose kernels overlap on the GPU race, so issue them in one stream order. */
 int  tl_reduce_cols_noalloc(int op, const float* in, float* out, int64_t rows, int64_t cols,
                             void* stream);
 /* out[0] = op over all n elements    (axis=None) */

@@ -23,7 +23,9 @@ constexpr int kFullMaxBlocks = 2048;  // upper bound of full-reduction blocks
 constexpr int kFullBlocksPerSm = 4;   // launch bounds keep 4 blocks of 256 resident per SM
 // Every scratch buffer starts with a fixed counter region; partials follow it,
 // so reductions of different kinds may share one scratch buffer in stream order.
-constexpr size_t kCounterBytes = 4096;
+// completion counters ahead of the partials: one per column stripe, enough
+// for 131072 columns on the one-column-per-lane path (32 columns a stripe)
+constexpr size_t kCounterBytes = 16384;
 constexpr unsigned kMaxColBlocks = kCounterBytes / 4;
 
 struct ArgVal {
@@ -559,31 +561,21 @@ int tl_reduce_full(int op, const float* in, float* out, int64_t n, void* scratch
 // runs).  The array is part of the module: every GPU that loads this library
 // holds it until process exit.  Every call shares it, so calls whose kernels
 // overlap on the GPU race; serialise them on one stream.
-#include <mutex>
-
 namespace tl {
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;  // 1 MiB per device
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
-
 // Device address of g_noalloc_scratch on the current device.  In host code
-// the array's name is only a host-side stand-in, so the address must come
-// from cudaGetSymbolAddress, once per device, with that device current.
+// the array's name is only a host-side stand-in, so the address comes from
+// cudaGetSymbolAddress with the device current.  It is looked up on every
+// call (cheap once the module is loaded), so it stays right after the
+// device's context is reset and the module reloaded.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  TL_CUDA_TRY(cudaGetDevice(&dev));
-  if (dev < 0 || dev >= 64) return TL_ERR_INVALID_ARG;
-  std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_addr[dev]) {
-    void* p = nullptr;
-    TL_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+  void* p = nullptr;
+  TL_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+  *out = p;
   return TL_OK;
 }
 
@@ -591,7 +583,7 @@ template <int OP>
 int launch_cols_noalloc(const float* in, float* out, int64_t rows, int64_t cols, cudaStream_t st) {
   const bool vec = (cols % 4 == 0) && aligned16(in);
   ColPlan p = col_plan(rows, cols, vec);
-  if (p.gx > kMaxColBlocks) return TL_ERR_INVALID_ARG;
+  if (p.gx > kMaxColBlocks) return TL_ERR_UNSUPPORTED;  // as tl_reduce_cols
   // fewer row chunks, so that the partials fit in the static array
   const size_t per_chunk = (size_t)cols * col_partial_bytes(OP);
   const size_t fit = (kNoAllocScratchBytes - kCounterBytes) / per_chunk;
