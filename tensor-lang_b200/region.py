@@ -35,6 +35,7 @@ from typing import Dict, List, Optional, Sequence, Tuple
 import numpy as np
 
 from . import runtime as rt
+from . import views as V
 
 BLOCK = 256
 UNROLL = 1          # units per thread per loop trip (more raised register use and lost
@@ -99,9 +100,13 @@ class Ref:
 
 @dataclass
 class Input:
-    key: str
-    access: str            # full | row | col | scalar | strided
+    key: Optional[str]
+    access: str            # full | row | col | scalar | strided | map
     strides: Tuple[int, ...] = ()  # for strided: per output axis, in elements
+    mapspec: tuple = ()    # for map: a views.py index map over buffer keys
+
+    def keys(self) -> List[str]:
+        return V.leaves(self.mapspec) if self.access == "map" else [self.key]
 
 
 @dataclass
@@ -117,16 +122,18 @@ class Seg:
     def total(self) -> int:
         return int(np.prod(self.shape)) if self.shape else 1
 
-    def add_input(self, key: str, in_shape: Sequence[int], access: Optional[str] = None) -> Ref:
+    def add_input(self, key: Optional[str], in_shape: Sequence[int], access: Optional[str] = None,
+                  mapspec: tuple = ()) -> Ref:
         in_shape = tuple(int(d) for d in in_shape)
         if access is None:
             access, strides = classify(self.shape, in_shape)
         else:
             strides = ()
         for i, inp in enumerate(self.inputs):
-            if inp.key == key and inp.access == access and inp.strides == strides:
+            if inp.key == key and inp.access == access and inp.strides == strides \
+                    and inp.mapspec == mapspec:
                 return Ref("in", i)
-        self.inputs.append(Input(key, access, strides))
+        self.inputs.append(Input(key, access, strides, tuple(mapspec)))
         return Ref("in", len(self.inputs) - 1)
 
     def const(self, v: float) -> Ref:
@@ -146,7 +153,7 @@ class Seg:
     def signature(self) -> str:
         parts = [f"S{self.shape}"]
         for i in self.inputs:
-            parts.append(f"I{i.access}{i.strides}")
+            parts.append(f"I{i.access}{i.strides}{i.mapspec}")
         for opc, args in self.body:
             parts.append(opc + "(" + ",".join(f"{a.kind}{a.idx}{a.value!r}" for a in args) + ")")
         for k, r in self.outputs:
@@ -210,8 +217,9 @@ class Region:
         keys: List[str] = []
         for s in self.segs:
             for i in s.inputs:
-                if i.key not in keys:
-                    keys.append(i.key)
+                for k in i.keys():
+                    if k not in keys:
+                        keys.append(k)
             for k, _ in s.outputs:
                 if k not in keys:
                     keys.append(k)
@@ -240,6 +248,8 @@ class Region:
             return False
         for i in s.inputs:
             if i.access == "strided" and i.strides[-1] not in (0, 1):
+                return False
+            if i.access == "map" and not V.vec4_ok(i.mapspec, len(s.shape)):
                 return False
         return True
 
@@ -270,7 +280,8 @@ class Region:
             if any(i.access == "col" for i in s.inputs):
                 out.append(f"      const long long c{x} = {e} % {C}LL;")
             strided = [ii for ii, i in enumerate(s.inputs) if i.access == "strided"]
-            if strided:
+            mapped = [ii for ii, i in enumerate(s.inputs) if i.access == "map"]
+            if strided or mapped:
                 out.append(f"      long long rem{x} = {e};")
                 for ax in reversed(range(len(shape))):
                     out.append(f"      const long long k{ax}{x} = rem{x} % {int(shape[ax])}LL; "
@@ -280,14 +291,23 @@ class Region:
                     out.append(f"      const long long o{ii}{x} = {' + '.join(terms) if terms else '0LL'};")
             return out
 
+        def map_load(m: tuple, x: str, four: bool) -> str:
+            """Expression loading one element (or float4) through index map ``m``."""
+            if m[0] == "aff":
+                terms = [f"{m[2]}LL"] + [f"k{ax}{x} * {st}LL" for ax, st in enumerate(m[3]) if st]
+                p = f"p{pidx[m[1]]} + ({' + '.join(terms)})"
+                return f"tl_ldc4({p})" if four else f"__ldg({p})"
+            return (f"(k{m[1]}{x} < {m[2]}LL ? {map_load(m[3], x, four)} : "
+                    f"{map_load(m[4], x, four)})")
+
         def is4(inp: Input) -> bool:
-            return vec and (inp.access in ("full", "col") or
+            return vec and (inp.access in ("full", "col", "map") or
                             (inp.access == "strided" and inp.strides[-1] == 1))
 
         def load_code(e: str, x: str) -> List[str]:
             out = []
             for ii, inp in enumerate(s.inputs):
-                p = f"p{pidx[inp.key]}"
+                p = f"p{pidx[inp.key]}" if inp.key is not None else ""
                 if inp.access == "full":
                     out.append(f"      const float4 v{ii}{x} = tl_ld4({p} + {e});" if vec
                                else f"      const float v{ii}{x} = __ldg({p} + {e});")
@@ -301,6 +321,9 @@ class Region:
                         out.append(f"      const float4 v{ii}{x} = tl_ldc4({p} + o{ii}{x});")
                     else:
                         out.append(f"      const float v{ii}{x} = __ldg({p} + o{ii}{x});")
+                elif inp.access == "map":
+                    t = "float4" if is4(inp) else "float"
+                    out.append(f"      const {t} v{ii}{x} = {map_load(inp.mapspec, x, is4(inp))};")
             return out
 
         def val(ref: Ref, lane: int, x: str) -> str:

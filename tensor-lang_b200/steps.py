@@ -14,6 +14,7 @@ from ctypes import c_float, c_int, c_int64, c_void_p
 from typing import Callable, Dict, List, Optional, Sequence, Tuple
 
 from . import runtime as rt
+from . import views as V
 from .region import Region, Seg, classify
 from .shapes import Shape, numel
 
@@ -34,14 +35,24 @@ class EW(Step):
     """One elementwise op over the iteration shape ``shape``.
 
     operands: ("name", tensor, access) with access in full|row|col|scalar|None
-    (None = NumPy broadcasting), or ("const", value).
+    (None = NumPy broadcasting), ("map", m) -- a view read through the index
+    map ``m`` (``views.py``) -- or ("const", value).
     """
 
     def __init__(self, out: str, shape: Shape, opcode: str, operands: list, label: str = ""):
         self.out, self.shape, self.opcode, self.operands = out, tuple(shape), opcode, operands
         self.label = label or f"{opcode}:{out}"
-        self.reads = [o[1] for o in operands if o[0] == "name"]
         self.writes = [out]
+        self._set_reads()
+
+    def _set_reads(self):
+        reads = []
+        for o in self.operands:
+            if o[0] == "name":
+                reads.append(o[1])
+            elif o[0] == "map":
+                reads += [n for n in V.leaves(o[1]) if n not in reads]
+        self.reads = reads
 
 
 class LibCall(Step):
@@ -138,6 +149,26 @@ class RegionStep(Step):
         bound = self.region.bind(ptrs)
         region, stream = self.region, P.stream
         return lambda: region.launch(bound, stream)
+
+
+class ViewStep(Step):
+    """A movement op (slice, transpose, reshape, concat).  ``resolve_views``
+    either folds it into the elementwise kernels that read it, as an index map
+    (``views.py``), or writes it: with ``fallback`` (the dedicated library
+    kernel or copy) when its inputs are in memory, else as a region copy
+    through the composed map."""
+
+    def __init__(self, view: V.View, fallback: Step):
+        self.view, self.fallback = view, fallback
+        self.out = view.out
+        self.reads, self.writes = list(view.sources), [view.out]
+        self.label = f"{view.kind}:{view.out}"
+
+    def bind(self, P):  # only reached when fusion is bypassed
+        return self.fallback.bind(P)
+
+    def compile(self, P):
+        self.fallback.compile(P)
 
 
 # ---------------------------------------------------------------------------
@@ -276,25 +307,29 @@ def kinfo_to_step(k: tuple, shapes: Dict[str, Shape], divisor_scale: Optional[di
                        [p, t], [name])
     if kind == "transpose_2d":  # :1949-1972
         t, rows, cols = k[2], int(k[4]), int(k[5])
-        return LibCall(f"transpose:{name}", "tl_transpose2d",
-                       [("ptr", t), ("ptr", name), ("int", rows), ("int", cols)], [t], [name])
+        lib = LibCall(f"transpose:{name}", "tl_transpose2d",
+                      [("ptr", t), ("ptr", name), ("int", rows), ("int", cols)], [t], [name])
+        return ViewStep(V.View("transpose", name, out, [t], ()), lib)
     if kind == "reshape":  # :2067-2086
-        return Copy(name, k[2])
+        return ViewStep(V.View("reshape", name, out, [k[2]], ()), Copy(name, k[2]))
     if kind == "slice_2d":  # :1112-1198
         t, rows, cols, r0, r1, c0, c1, orows, ocols = k[2], *[int(v) for v in k[4:12]]
-        return LibCall(f"slice:{name}", "tl_slice2d",
-                       [("ptr", t), ("ptr", name), ("int", cols), ("int", r0), ("int", c0),
-                        ("int", orows), ("int", ocols)], [t], [name])
+        lib = LibCall(f"slice:{name}", "tl_slice2d",
+                      [("ptr", t), ("ptr", name), ("int", cols), ("int", r0), ("int", c0),
+                       ("int", orows), ("int", ocols)], [t], [name])
+        return ViewStep(V.View("slice", name, out, [t], (r0, c0)), lib)
     if kind == "slice_1d":  # :1200-1240
         t, start, n = k[2], int(k[4]), int(k[5])
-        return LibCall(f"slice:{name}", "tl_slice2d",
-                       [("ptr", t), ("ptr", name), ("int", max(1, start + n)), ("int", 0),
-                        ("int", start), ("int", 1 if n > 0 else 0), ("int", n)], [t], [name])
+        lib = LibCall(f"slice:{name}", "tl_slice2d",
+                      [("ptr", t), ("ptr", name), ("int", max(1, start + n)), ("int", 0),
+                       ("int", start), ("int", 1 if n > 0 else 0), ("int", n)], [t], [name])
+        return ViewStep(V.View("slice", name, out, [t], (start,)), lib)
     if kind == "concat_axis0":  # :2092-2132
         a, b, r1, r2, cols = k[2], k[3], int(k[4]), int(k[5]), int(k[6])
-        return LibCall(f"concat:{name}", "tl_concat_rows",
-                       [("ptr", a), ("ptr", b), ("ptr", name), ("int", r1), ("int", r2),
-                        ("int", cols)], [a, b], [name])
+        lib = LibCall(f"concat:{name}", "tl_concat_rows",
+                      [("ptr", a), ("ptr", b), ("ptr", name), ("int", r1), ("int", r2),
+                       ("int", cols)], [a, b], [name])
+        return ViewStep(V.View("concat0", name, out, [a, b], ()), lib)
     raise NotImplementedError(f"no backend dispatch for kernel_info {k[0]!r}")
 
 
@@ -314,6 +349,7 @@ def fuse(steps: List[Step], shapes: Dict[str, Shape], live: set, read_count: Dic
     no data hazard between them become segments of one launch.  ``canon``
     maps a name to the tensor whose buffer it shares (in-place updates).
     """
+    steps = resolve_views(steps, shapes, live, read_count, canon or {})
     out: List[Step] = []
     run: List[EW] = []
 
@@ -326,6 +362,8 @@ def fuse(steps: List[Step], shapes: Dict[str, Shape], live: set, read_count: Dic
         if isinstance(st, EW):
             if run and run[0].shape != st.shape:
                 flush()
+            elif run and _maps_read_run(st, run):
+                flush()  # a view of a value this run computes: written first
             run.append(st)
         else:
             flush()
@@ -351,6 +389,73 @@ def fuse(steps: List[Step], shapes: Dict[str, Shape], live: set, read_count: Dic
         else:
             result.append(st)
     return result
+
+
+def _maps_read_run(st: EW, run: List[EW]) -> bool:
+    written = {op.out for op in run}
+    return any(o[0] == "map" and set(V.leaves(o[1])) & written for o in st.operands)
+
+
+def resolve_views(steps: List[Step], shapes: Dict[str, Shape], live: set,
+                  read_count: Dict[str, int], canon: Dict[str, str]) -> List[Step]:
+    """Fold each ``ViewStep`` into the elementwise steps that read it, as an
+    index map, or write it where it stands.
+
+    A view folds when nothing else needs it in memory: it is not live, every
+    read of it in the whole program is by a later step of this list that is
+    either an elementwise op reading it element for element (same shape,
+    ``full`` access) or another view that composes with it, and no step up to
+    its last reader writes the tensors the map reads."""
+    c = lambda n: canon.get(n, n)  # noqa: E731
+    maps: Dict[str, tuple] = {}
+    out: List[Step] = []
+    for i, st in enumerate(steps):
+        if isinstance(st, ViewStep):
+            v = st.view
+            in_maps = [maps.get(src) or V.identity(shapes[src], src) for src in v.sources]
+            m = v.build(in_maps, [shapes[src] for src in v.sources])
+            if m is not None and _view_folds(v.out, m, steps, i, shapes, live, read_count, c):
+                maps[v.out] = m
+                continue
+            if m is None or any(src in maps for src in v.sources):
+                if m is None:
+                    raise NotImplementedError(f"{st.label}: a view of a view that does not compose")
+                out.append(EW(v.out, v.out_shape, "copy", [("map", m)], label=f"{st.label}(map)"))
+            else:
+                out.append(st.fallback)
+            continue
+        if isinstance(st, EW) and any(o[0] == "name" and o[1] in maps for o in st.operands):
+            ops = [("map", maps[o[1]]) if o[0] == "name" and o[1] in maps else o
+                   for o in st.operands]
+            st = EW(st.out, st.shape, st.opcode, ops, label=st.label)
+        out.append(st)
+    return out
+
+
+def _view_folds(name, m, steps, i, shapes, live, read_count, c) -> bool:
+    if name in live:
+        return False
+    shape = tuple(shapes[name])
+    nreads, last = 0, i
+    for j in range(i + 1, len(steps)):
+        st = steps[j]
+        n = st.reads.count(name)
+        if not n:
+            continue
+        nreads += n
+        last = j
+        if isinstance(st, ViewStep):
+            if st.view.kind == "reshape" and not V.is_whole(m, shape):
+                return False
+            continue
+        if not isinstance(st, EW) or tuple(st.shape) != shape:
+            return False
+        if any(o[0] == "name" and o[1] == name and o[2] != "full" for o in st.operands):
+            return False
+    if nreads == 0 or nreads != read_count.get(name, 0):
+        return False
+    srcs = {c(n) for n in V.leaves(m)}
+    return not any(c(w) in srcs for st in steps[i + 1:last + 1] for w in st.writes)
 
 
 class _RunMarker:
@@ -405,6 +510,12 @@ class _RunGroup:
                 for o in op.operands:
                     if o[0] == "const":
                         args.append(seg.const(o[1]))
+                        continue
+                    if o[0] == "map":
+                        keyed = V.rename(o[1], key)
+                        ref = seg.add_input(None, shape, "map", keyed)
+                        reads.update(V.leaves(o[1]))
+                        args.append(ref)
                         continue
                     nm, acc = o[1], o[2]
                     if nm in cur and numel(shapes[nm]) == numel(shape):
