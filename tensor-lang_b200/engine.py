@@ -28,6 +28,7 @@ import numpy as np
 
 from . import runtime as rt
 from .autograd import BackwardPlanner, Node, grad_name
+from .dataio import check_shape, load_data_file
 from .epilogue import fuse_gemm_epilogues
 from .pairs import plan_gemm_pairs
 from .kernel_generator import KernelGenerator
@@ -291,9 +292,10 @@ class Program:
             return np.asarray(e["data"], dtype=np.float32).reshape(shp)
         if e["type"] == "load":
             src = self.load_files.get(e["file_path"])
-            if src is None:
-                src = np.load(e["file_path"])
-            return np.asarray(src, dtype=np.float32).reshape(shp)
+            if src is not None:
+                return np.asarray(src, dtype=np.float32).reshape(shp)
+            data, _meta = load_data_file(e["file_path"], e.get("array_name"))
+            return check_shape(name, e["file_path"], data, shp)
         raise ValueError(e["type"])
 
     def _let_step(self, node) -> Optional[Step]:

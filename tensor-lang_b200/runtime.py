@@ -20,7 +20,9 @@ import numpy as np
 
 PKG_DIR = Path(__file__).resolve().parent
 LIB_PATH = PKG_DIR / "libtlb200.so"
-JIT_DIR = PKG_DIR / "_jit"
+# compiled fused-region cubins, keyed by a hash of their source; TL_JIT_DIR
+# moves the cache (an empty directory gives a cold first run)
+JIT_DIR = Path(os.environ.get("TL_JIT_DIR", str(PKG_DIR / "_jit")))
 
 TL_ERR_INVALID_ARG = 1001
 TL_ERR_ALIGNMENT = 1002
