@@ -163,6 +163,69 @@ def reductions_inputs(R=16384, C=4096, seed=0) -> Dict[str, np.ndarray]:
             "xi1": tie_copy(x, 1, False, rng), "xi0": tie_copy(x, 0, False, rng)}
 
 
+def unary_vjp(op="gelu", R=4096, C=4096) -> list:
+    """``y = op(x); loss = mse_loss(y, T); backward(loss)`` with ``x`` tracked:
+    the activation's forward and its VJP (autograd.py:540-561 for relu,
+    sigmoid and tanh; gelu and swish have no reference VJP)."""
+    return [
+        _let("x", _fill((R, C)), (R, C), grad=True),
+        _let("T", _fill((R, C)), (R, C)),
+        _let("y", _call(op, "x")),
+        _let("loss", _call("mse_loss", "y", "T")),
+        {"type": "backward", "loss_tensor": "loss"},
+    ]
+
+
+def unary_vjp_inputs(R=4096, C=4096, seed=0) -> Dict[str, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((R, C)) * 2.0).astype(np.float32)
+    T = rng.standard_normal((R, C)).astype(np.float32)
+    return {"x": x, "T": T}
+
+
+def layer_norm_vjp(R=16384, C=4096, eps=0.00001) -> list:
+    """``y = layer_norm(x, axis=1); loss = mse_loss(y, T); backward(loss)``:
+    the row normalisation and its VJP (autograd.py:649-674)."""
+    return [
+        _let("x", _fill((R, C)), (R, C), grad=True),
+        _let("T", _fill((R, C)), (R, C)),
+        _let("y", {"type": "layer_norm", "tensor": "x", "axis": 1, "eps": float(eps)}),
+        _let("loss", _call("mse_loss", "y", "T")),
+        {"type": "backward", "loss_tensor": "loss"},
+    ]
+
+
+def layer_norm_vjp_inputs(R=16384, C=4096, seed=0) -> Dict[str, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    # rows with their own offset and scale, so the VJP's mean and variance
+    # terms both matter
+    x = (rng.standard_normal((R, C)) * rng.uniform(0.5, 2.0, (R, 1))
+         + rng.standard_normal((R, 1))).astype(np.float32)
+    T = rng.standard_normal((R, C)).astype(np.float32)
+    return {"x": x, "T": T}
+
+
+def norms(R=16384, C=4096, eps=0.00001) -> list:
+    """batch_norm with running statistics (kernel_generator.py:1978-2011) and
+    instance_norm per row (:2017-2061) of one matrix."""
+    return [
+        _let("x", _fill((R, C)), (R, C)),
+        _let("rm", _fill((C,)), (C,)),
+        _let("rv", _fill((C,)), (C,)),
+        _let("bn", {"type": "batch_norm", "tensor": "x", "running_mean": "rm",
+                    "running_var": "rv", "eps": float(eps)}),
+        _let("inn", {"type": "instance_norm", "tensor": "x", "eps": float(eps)}),
+    ]
+
+
+def norms_inputs(R=16384, C=4096, seed=0) -> Dict[str, np.ndarray]:
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((R, C)) * 1.5 + 0.25).astype(np.float32)
+    rm = (rng.standard_normal(C) * 0.3).astype(np.float32)
+    rv = rng.uniform(0.5, 3.0, C).astype(np.float32)
+    return {"x": x, "rm": rm, "rv": rv}
+
+
 # ---------------------------------------------------------------------------
 # linear layer with autograd
 # ---------------------------------------------------------------------------
