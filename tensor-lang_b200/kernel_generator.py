@@ -7,7 +7,7 @@ key of ``TensorCompiler._execute_single_kernel`` (compiler.py:365-673).
 
 This class has the same method names, argument lists and ``kernel_info``
 tuples (checked against the reference generator in
-``tests/test_kernel_generator.py``).  The source string is empty: the kernels
+``tests/test_cpu_boundary.py``).  The source string is empty: the kernels
 are the prebuilt sm_100a kernels of libtlb200 and the fused elementwise
 regions the backend generates itself, so nothing per-op needs compiling.
 

@@ -3,7 +3,7 @@
 Run here (where the TensorLang reference checkout is readable), never on the
 GPU host:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <checkout of the reference>
 
 What it produces (all small JSON, committed):
 
@@ -48,9 +48,9 @@ import io
 import json
 import os
 import re
-import shutil
 import subprocess
 import sys
+import tempfile
 import types
 from pathlib import Path
 
@@ -58,7 +58,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-SCRATCH = REPO / "_work" / "golden_run"
+# working directory of one run (a fresh temporary directory, set by
+# run_reference_programs): the reference writes its kernel.cu and cache there
+SCRATCH: Path = Path()
 
 
 # ---------------------------------------------------------------------------
@@ -447,9 +449,8 @@ def run_reference_programs(ref: Path):
     import tensorlang.compiler as tlc
     from tensorlang.kernel_generator import KernelGenerator
 
-    if SCRATCH.exists():
-        shutil.rmtree(SCRATCH)
-    SCRATCH.mkdir(parents=True)
+    global SCRATCH
+    SCRATCH = Path(tempfile.mkdtemp(prefix="tl_golden_"))
     (SCRATCH / "tensorlang.lark").symlink_to(ref / "tensorlang.lark")
     (SCRATCH / "tests").symlink_to(ref / "tests")
     os.chdir(SCRATCH)
@@ -717,7 +718,9 @@ def autograd_cases(ref: Path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("TL_REFERENCE"),
+                    required="TL_REFERENCE" not in os.environ,
+                    help="checkout of the TensorLang reference (or set TL_REFERENCE)")
     args = ap.parse_args()
     ref = Path(args.reference).resolve()
     progs = run_reference_programs(ref)
