@@ -42,6 +42,9 @@ B_GLOBAL, D_IN, D_H, N_CLS = 65536, 1024, 4096, 10
 FLOP_PER_STEP = 7_712_686_521_792  # fwd 3 GEMMs + dW 3 + dX of layers 2,3
 FUSED_N = 8192
 FUSED_BYTES = 805_371_904  # read x, write y and m, plus s and b
+C4_SHAPE = (8192, 4096, 4096)  # linear layer X[8192,4096] @ W[4096,4096]
+C4_FLOP = 3 * 2 * 8192 * 4096 * 4096  # forward, dW, dX
+METRIC = "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)"
 # GEMM operand schemes (tl_gemm_set_scheme): code, description, and bf16
 # MMA-times per fp32 product -- the scheme's ceiling is the bf16 peak / that
 GEMM_SCHEMES = {
@@ -138,44 +141,106 @@ def dist_env():
 # CPU baseline: the reference's NumPy execution (float32 oracle restatement)
 # ---------------------------------------------------------------------------
 
-def cpu_mlp_step_time(rows: int, reps: int = 1):
+def _oracle():
     from oracle import OracleProgram
     from __graft_entry__ import load_package
     tl = load_package()
+    return tl, OracleProgram
+
+
+def _env(tl, ast):
+    return {k: {"shape": v} for k, v in tl.shapes.complete_env(ast, {}).items()}
+
+
+def cpu_mlp_step_times(steps: int, warmup: int):
+    """Seconds of each full-batch (65536-row) training step of the float32
+    oracle, after ``warmup`` untimed steps."""
+    tl, OracleProgram = _oracle()
     pr = tl.programs
-    ast = pr.mlp3_train(B=rows, I=D_IN, H=D_H, C=N_CLS, epochs=1)
-    feeds = pr.mlp3_inputs(B=rows, I=D_IN, H=D_H, C=N_CLS, seed=0)
-    env = {k: {"shape": v} for k, v in tl.shapes.complete_env(ast, {}).items()}
+    ast = pr.mlp3_train(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, epochs=1)
+    feeds = pr.mlp3_inputs(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, seed=0)
+    env = _env(tl, ast)
     times = []
-    for _ in range(reps):
+    for i in range(warmup + steps):
         t0 = time.perf_counter()
         OracleProgram(ast, env, dtype=np.float32, feeds=feeds).run()
-        times.append(time.perf_counter() - t0)
-    return min(times)
+        if i >= warmup:
+            times.append(time.perf_counter() - t0)
+    return times
+
+
+def _best(fn, reps):
+    best = float("inf")
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        fn()
+        best = min(best, time.perf_counter() - t0)
+    return best
+
+
+def cpu_configs():
+    """The float32 oracle on the other workloads (best of 3 for the single
+    ops, best of 20 for the small training step, one run of the linear layer)."""
+    tl, OracleProgram = _oracle()
+    pr = tl.programs
+    out = {}
+    ast, feeds = pr.mlp2_step(), pr.mlp2_inputs(seed=0)
+    env = _env(tl, ast)
+    t = _best(lambda: OracleProgram(ast, env, dtype=np.float32, feeds=feeds).run(), 20)
+    out["mlp2_step_64x128"] = {"us_per_step": t * 1e6, "protocol": "best of 20"}
+    ast, feeds = pr.fused_chain(FUSED_N), pr.fused_chain_inputs(FUSED_N, seed=0)
+    env = _env(tl, ast)
+    t = _best(lambda: OracleProgram(ast, env, dtype=np.float32, feeds=feeds).run(), 3)
+    out["fused_chain_8192"] = {"s": t, "GB/s": FUSED_BYTES / t / 1e9, "protocol": "best of 3"}
+    R, C_ = 16384, 4096
+    feeds = pr.reductions_inputs(R, C_, seed=0)
+    ops = {}
+    from oracle.tl_oracle import op_forward
+    for name, op, ax in pr.REDUCTION_OPS + [("sm", "softmax", 1), ("ln", "layer_norm", 1)]:
+        src = {"argmax1": "xa1", "argmax0": "xa0", "argmin1": "xi1", "argmin0": "xi0"}.get(name, "x")
+        expr = {"type": op, "tensor": src, "axis": ax}
+        if op == "layer_norm":
+            expr["eps"] = 0.00001
+        t = _best(lambda: op_forward(expr, feeds, np.float32), 3)
+        nbytes = 4.0 * R * C_ * (2 if op in ("softmax", "layer_norm") else 1)
+        ops[f"{op}(axis={ax})" if ax is not None else f"{op}(all)"] = {
+            "s": t, "GB/s": nbytes / t / 1e9}
+    out["reductions_16384x4096"] = {"ops": ops, "protocol": "best of 3 per op"}
+    M, K, N = C4_SHAPE
+    ast, feeds = pr.linear_layer(M, K, N), pr.linear_layer_inputs(M, K, N, seed=0)
+    env = _env(tl, ast)
+    t = _best(lambda: OracleProgram(ast, env, dtype=np.float32, feeds=feeds).run(), 1)
+    out["linear_layer_8192x4096x4096"] = {"s": t, "GFLOP/s": C4_FLOP / t / 1e9,
+                                          "protocol": "one forward + backward"}
+    return out
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
-    rows = args.cpu_rows
     cores = os.cpu_count() or 1
-    for _ in range(max(1, args.warmup)):
-        cpu_mlp_step_time(rows)
-    samples = [cpu_mlp_step_time(rows) for _ in range(max(1, args.steps))]
-    t = float(np.mean(samples)) * (B_GLOBAL / rows)  # seconds per full-batch step
+    # full-batch steps cost ~10 s each on the host: at most 2 timed steps
+    # after 1 warm-up step, whatever --steps/--warmup ask for
+    steps, warmup = max(1, min(args.steps, 2)), min(args.warmup, 1)
+    samples = cpu_mlp_step_times(steps, warmup)
+    t = float(np.mean(samples))
     value = 1.0 / t
     line = {
-        "impl": "reference", "metric": "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)",
-        "value": value, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
-        "warmup": args.warmup, "ms_per_step": t * 1000.0, "higher_is_better": True,
+        "impl": "reference", "metric": METRIC,
+        "value": value, "unit": "steps/s", "n_gpus": world, "steps": steps,
+        "warmup": warmup, "steps_requested": args.steps, "warmup_requested": args.warmup,
+        "ms_per_step": t * 1000.0, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL, "dims": [D_IN, D_H, D_H, N_CLS],
                    "parallelism": "host numpy", "l2": "inputs larger than L2"},
         "cpu_baseline": {"value": value, "unit": "steps/s", "cores": cores, "kind": "port",
-                         "sample": f"one training step on {rows} of the {B_GLOBAL} rows, "
-                                   f"scaled x{B_GLOBAL // rows}; mean of {len(samples)}"},
+                         "sample": f"{steps} full-batch ({B_GLOBAL}-row) training steps of the "
+                                   f"float32 NumPy oracle after {warmup} warm-up step; "
+                                   f"mean {t:.2f} s per step"},
         "e2e": {"value": value, "unit": "steps/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
+    if not args.no_cpu_configs:
+        line["configs"] = cpu_configs()
     print(json.dumps(line), flush=True)
     return 0
 
@@ -277,6 +342,193 @@ def fused_op_bench(tl, dev, reps=20):
     return res
 
 
+def build_training(tl, comm, dev, rank, world, epochs):
+    """The benchmark program on this rank's shard, prepared, with its first
+    iteration run eagerly; returns (program, loop, feeds, kernel launches per
+    iteration)."""
+    from tensor_lang_b200 import dp
+    rt = tl.runtime
+    b = B_GLOBAL // world
+    pr = tl.programs
+    ast = pr.mlp3_train(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, epochs=epochs)
+    feeds = pr.mlp3_inputs(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, seed=0, rows=(rank * b, (rank + 1) * b))
+    D = dp.DataParallelProgram(ast, None, comm, device=dev, feeds=feeds, fetch=["loss", "W3"])
+    P = D.program
+    P.prepare()
+    loop = P.loops[0]
+    # first iteration eagerly (counts kernel launches), then capture the graph
+    rt.launch_count(reset=True)
+    loop.run_eager()
+    n_eager = rt.launch_count(reset=True)
+    loop.run_hoisted()  # hoisted steps run outside the per-iteration graph
+    launches_per_step = n_eager - rt.launch_count()
+    loop.capture()
+    return P, loop, feeds, launches_per_step
+
+
+def hidden_gemm(tl, P, M, scheme, check: bool):
+    """The hidden-layer product a1[M,4096] @ W2 + b2 of the program, timed
+    alone (CUDA events, 5 calls); with ``check``, the error of its result on
+    one row per 128-row block and one column per 256-column block against a
+    float64 evaluation of the same rows and columns, relative to max|ref|."""
+    rt = tl.runtime
+    L = rt.lib()
+    N = K = D_H
+    stream = P.stream
+    args = (M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("a2"), N)
+    gemm = lambda: rt.check(L.tl_gemm(0, 0, *args, P.ptr("b2"), 0, 0, stream), "gemm")  # noqa: E731
+    gemm()
+    P.sync()
+    ms = time_events(tl, stream, gemm, 5)
+    on_tc = L.tl_gemm_path(0, 0, *args) == 0
+    path = f"{GEMM_SCHEMES[scheme][1]}, CTA-pair 256x256 tiles" if on_tc else "CUDA-core fp32"
+    plan = (ctypes.c_int * 4)()
+    rt.check(L.tl_gemm_tc_plan(M, N, K, plan), "gemm plan")
+    tflops = 2.0 * M * N * K / (ms * 1e-3) / 1e12
+    _, bf16, _, src = peaks()
+    ceiling = bf16 / GEMM_SCHEMES[scheme][2]
+    res = {"bound": "tensor", "kernel": f"GEMM {M}x{N}x{K} ({path})",
+           "achieved": tflops, "peak": bf16, "unit": "TFLOP/s", "frac": tflops / bf16,
+           "peak_source": f"{src} bf16 dense (burst)",
+           # captured for the one-GPU launch (65536 rows) only
+           "traffic": GEMM_TRAFFIC_BYTES.get(scheme) if M == B_GLOBAL else None,
+           "scheme_ceiling": ceiling, "frac_of_scheme_ceiling": tflops / ceiling,
+           "ms_per_call": ms,
+           "launch": {"k_splits": plan[1], "tiles_per_cluster": plan[2], "clusters": plan[3]}}
+    if check:
+        a1, C = P.read("a1"), P.read("a2")
+        W2, b2 = P.read("W2").astype(np.float64), P.read("b2").astype(np.float64)
+        rng = np.random.default_rng(0)
+        rows = np.arange(0, M, 128) + rng.integers(0, 128, (M + 127) // 128)
+        rows = np.minimum(rows, M - 1)
+        cols = np.minimum(np.arange(0, N, 256) + rng.integers(0, 256, (N + 255) // 256), N - 1)
+        rr = a1[rows].astype(np.float64) @ W2 + b2
+        rc = np.empty((M, len(cols)))
+        for r in range(0, M, 8192):
+            rc[r:r + 8192] = a1[r:r + 8192].astype(np.float64) @ W2[:, cols] + b2[cols]
+        scale = max(np.abs(rr).max(), np.abs(rc).max())
+        err = max(np.abs(C[rows] - rr).max(), np.abs(C[:, cols] - rc).max())
+        res["max_err_of_max_abs"] = float(err / scale)
+        res["error_check"] = (f"{len(rows)} rows x {N} and {M} x {len(cols)} columns of the "
+                              f"result against float64")
+    return res
+
+
+def time_training(tl, loop, stream, steps, clocks=None):
+    def timed_step():
+        loop.replay(1)
+        if clocks is not None:
+            clocks.sample()  # host-side sample while the step runs on the device
+    return time_events(tl, stream, timed_step, steps)
+
+
+def gpu_configs(tl, dev):
+    """The other workloads on this GPU (CUDA events on the program's stream,
+    after 3 untimed runs): the 2-layer training step, the reductions and
+    normalisations of [16384,4096], one forward + backward of the linear layer."""
+    rt = tl.runtime
+    pr = tl.programs
+    hbm, _, _, src = peaks()
+    out = {}
+    P = tl.Program(pr.mlp2_step(), None, feeds=pr.mlp2_inputs(seed=0),
+                   fetch=["loss", "W1_new", "b1_new", "W2_new", "b2_new"], device=dev)
+    P.prepare()
+    for _ in range(3):
+        P.execute()
+    ms = time_events(tl, P.stream, P.execute, 50)
+    out["mlp2_step_64x128"] = {"us_per_step": ms * 1e3, "launches": len(P._all_steps()),
+                               "note": "one launch per step from the host, no graph: launch-bound"}
+    P.free()
+    R, C_ = 16384, 4096
+    P = tl.Program(pr.reductions(R, C_), None, feeds=pr.reductions_inputs(R, C_),
+                   fetch=[n for n, _, _ in pr.REDUCTION_OPS] + ["sm", "ln"], device=dev)
+    P.prepare()
+    ops = {}
+    for s in P._all_steps():
+        call = s.bind(P)
+        for _ in range(3):
+            call()
+        P.sync()
+        t = time_events(tl, P.stream, call, 20)
+        two_way = s.label.split(":")[0] in ("softmax", "layer_norm_2d")
+        gbs = 4.0 * R * C_ * (2 if two_way else 1) / (t * 1e-3) / 1e9
+        ops[s.label] = {"GB/s": gbs, "frac": gbs / hbm}
+    P.free()
+    fr = [v["frac"] for v in ops.values()]
+    out["reductions_16384x4096"] = {"ops": ops, "frac_min": min(fr), "frac_max": max(fr),
+                                    "peak": hbm, "peak_source": src}
+    M, K, N = C4_SHAPE
+    P = tl.Program(pr.linear_layer(M, K, N), None, feeds=pr.linear_layer_inputs(M, K, N, seed=0),
+                   fetch=["loss", "W_grad", "b_grad", "X_grad"], device=dev)
+    P.prepare()
+    for _ in range(3):
+        P.execute()
+    ms = time_events(tl, P.stream, P.execute, 5)
+    out["linear_layer_8192x4096x4096"] = {"ms": ms, "TFLOP/s": C4_FLOP / (ms * 1e-3) / 1e12,
+                                          "work": "forward, relu, mse, dW, db, dX"}
+    P.free()
+    return out
+
+
+FIRST_RUN = r"""
+import json, sys, time
+t0 = time.perf_counter()
+sys.path.insert(0, sys.argv[1])
+from __graft_entry__ import load_package
+tl = load_package()
+tl.load_library()
+t1 = time.perf_counter()
+pr = tl.programs
+P = tl.Program(pr.mlp2_step(), None, feeds=pr.mlp2_inputs(seed=0), fetch=["loss"])
+P.run()
+t2 = time.perf_counter()
+Q = tl.Program(pr.mlp2_step(), None, feeds=pr.mlp2_inputs(seed=1), fetch=["loss"])
+Q.run()
+t3 = time.perf_counter()
+print(json.dumps({"load_s": t1 - t0, "first_program_s": t2 - t1, "second_program_s": t3 - t2}))
+"""
+
+
+def first_run_latency():
+    """Wall time from process start to the first result of the 2-layer training
+    step program, in fresh processes: cold (empty fused-region cubin cache, so
+    every region is compiled by NVRTC) and warm (the cubins on disk)."""
+    import tempfile
+    out = {}
+    with tempfile.TemporaryDirectory(prefix="tl_jit_") as jit:
+        env = dict(os.environ, TL_JIT_DIR=jit)
+        for kind in ("cold", "warm"):
+            t0 = time.perf_counter()
+            r = subprocess.run([sys.executable, "-c", FIRST_RUN, str(REPO)], env=env,
+                               capture_output=True, text=True, timeout=300)
+            wall = time.perf_counter() - t0
+            if r.returncode != 0:
+                raise RuntimeError(f"first-run probe failed: {r.stderr[-2000:]}")
+            rec = json.loads(r.stdout.strip().splitlines()[-1])
+            rec["process_wall_s"] = wall
+            out[kind] = rec
+    out["program"] = "2-layer MLP training step [64,128] (parse-free: AST built in Python)"
+    return out
+
+
+def contract_scheme(tl, comm, dev, args):
+    """The same step with the GEMMs in the split-TF32 scheme (TF32 hi*hi plus
+    one bf16 pair MMA for the corrections): steps/s and the hidden GEMM."""
+    set_gemm_scheme(tl, "tf32bf16")
+    try:
+        P, loop, _, _ = build_training(tl, comm, dev, 0, 1, epochs=1 + 3 + 10)
+        for _ in range(3):
+            loop.replay(1)
+        P.sync()
+        ms = time_training(tl, loop, P.stream, 10)
+        g = hidden_gemm(tl, P, B_GLOBAL, "tf32bf16", check=True)
+        P.free()
+    finally:
+        set_gemm_scheme(tl, args.gemm_scheme)
+    return {"gemm": GEMM_SCHEMES["tf32bf16"][1], "value": 1000.0 / ms, "unit": "steps/s",
+            "ms_per_step": ms, "steps": 10, "warmup": 3, "roofline": g}
+
+
 def run_ours(args, rank, world, local):
     from __graft_entry__ import load_package
     tl = load_package()
@@ -292,23 +544,9 @@ def run_ours(args, rank, world, local):
     comm = dp.Communicator(rdv)
 
     b = B_GLOBAL // world
-    r0, r1 = rank * b, (rank + 1) * b
-    pr = tl.programs
-    ast = pr.mlp3_train(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, epochs=1 + args.warmup + args.steps)
-    feeds = pr.mlp3_inputs(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, seed=0, rows=(r0, r1))
-    D = dp.DataParallelProgram(ast, None, comm, device=dev, feeds=feeds, fetch=["loss", "W3"])
-    P = D.program
-    P.prepare()
-    loop = P.loops[0]
+    P, loop, feeds, launches_per_step = build_training(tl, comm, dev, rank, world,
+                                                       epochs=1 + args.warmup + args.steps)
     stream = P.stream
-
-    # first iteration eagerly (counts kernel launches), then capture the graph
-    rt.launch_count(reset=True)
-    loop.run_eager()
-    n_eager = rt.launch_count(reset=True)
-    loop.run_hoisted()  # hoisted steps run outside the per-iteration graph
-    launches_per_step = n_eager - rt.launch_count()
-    loop.capture()
     for _ in range(args.warmup):
         loop.replay(1)
     comm.wait(stream)
@@ -317,12 +555,7 @@ def run_ours(args, rank, world, local):
     clocks = Clocks(dev)
     rdv.barrier()
     clocks.start()
-
-    def timed_step():
-        loop.replay(1)
-        clocks.sample()  # host-side sample while the step runs on the device
-
-    ms = time_events(tl, stream, timed_step, args.steps)
+    ms = time_training(tl, loop, stream, args.steps, clocks)
     clk = clocks.stop()
     rdv.barrier()
     all_ms = rdv.gather(ms)
@@ -330,52 +563,42 @@ def run_ours(args, rank, world, local):
     # e2e through the public API: every step's batch comes from pinned host
     # memory and every step's loss goes back to the host
     xs, ts = feeds["x"], feeds["t"]
-    L = rt.lib()
     e2e_steps = max(1, min(args.steps, 10))
     e2e_ms = e2e_time(tl, rt.Device.get(dev), loop, stream, P.ptr("x"), P.ptr("t"), P.ptr("loss"),
                       xs, ts, e2e_steps)
     rdv.barrier()
     all_e2e = rdv.gather(e2e_ms)
-
-    # dominant kernel: the hidden-layer GEMM (b x 4096 x 4096), timed alone
-    M, N, K = b, D_H, D_H
-    gemm = lambda: rt.check(L.tl_gemm(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("a2"),  # noqa: E731
-                                       N, P.ptr("b2"), 0, 0, stream), "gemm")
-    gemm()
-    P.sync()
-    g_ms = time_events(tl, stream, gemm, 5)
-    on_tc = L.tl_gemm_path(0, 0, M, N, K, P.ptr("a1"), K, P.ptr("W2"), N, P.ptr("a2"), N) == 0
-    path = (f"{GEMM_SCHEMES[args.gemm_scheme][1]}, CTA-pair 256x256 tiles"
-            if on_tc else "CUDA-core fp32")
-    plan = (ctypes.c_int * 4)()
-    rt.check(L.tl_gemm_tc_plan(M, N, K, plan), "gemm plan")
-    gemm_plan = {"k_splits": plan[1], "tiles_per_cluster": plan[2], "clusters": plan[3]}
     loss = float(P.read("loss").reshape(-1)[0])
 
-    fused = None
-    if world == 1 and not args.no_fused:
-        fused = fused_op_bench(tl, dev)
+    # dominant kernel: the hidden-layer GEMM (b x 4096 x 4096), timed alone
+    roof = hidden_gemm(tl, P, b, args.gemm_scheme, check=(rank == 0 and not args.no_check))
+    P.free()
+
+    extra = {}
+    if world == 1 and not args.no_configs:
+        extra["contract_scheme"] = contract_scheme(tl, comm, dev, args)
+        extra["fused_op"] = fused_op_bench(tl, dev)
+        extra["configs"] = gpu_configs(tl, dev)
+        extra["first_run"] = first_run_latency()
 
     if rank == 0:
         cpu = None
         if not args.no_cpu:
-            rows = args.cpu_rows
-            t = cpu_mlp_step_time(rows) * (B_GLOBAL / rows)
+            t = cpu_mlp_step_times(1, 0)[0]
             cpu = {"value": 1.0 / t, "unit": "steps/s", "cores": os.cpu_count() or 1, "kind": "port",
-                   "sample": f"float32 NumPy oracle: one training step on {rows} of {B_GLOBAL} rows, "
-                             f"scaled x{B_GLOBAL // rows}"}
+                   "sample": f"one full-batch ({B_GLOBAL}-row) training step of the float32 NumPy "
+                             f"oracle ({t:.2f} s)"}
         ms_max = max(all_ms)
-        hbm, bf16, bf16s, src = peaks()
-        ceiling = bf16 / GEMM_SCHEMES[args.gemm_scheme][2]
-        tflops = 2.0 * M * N * K / (g_ms * 1e-3) / 1e12
+        scheme = GEMM_SCHEMES[args.gemm_scheme]
         line = {
-            "metric": "MLP train steps/sec (3-layer 1024-4096-4096-10, batch 65536)",
+            "metric": METRIC,
             "value": 1000.0 / ms_max, "unit": "steps/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_max, "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": f"f32 ({args.gemm_scheme} split GEMMs)", "data": "synthetic",
             "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL,
                        "per_gpu_batch": b, "dims": [D_IN, D_H, D_H, N_CLS],
-                       "parallelism": f"dp{world}", "gemm": path,
+                       "parallelism": f"dp{world}", "gemm": f"{scheme[1]}, CTA-pair 256x256 tiles",
                        "l2": "inputs larger than L2 (no flush)"},
             "model_tflops": FLOP_PER_STEP / (ms_max * 1e-3) / 1e12,
             "loss_rank0": loss,
@@ -383,14 +606,7 @@ def run_ours(args, rank, world, local):
             # flops; per fp32 product BF16X3 issues three bf16 products (ceiling
             # bf16 / 3), TF32+bf16 one TF32 product at half the bf16 rate and two
             # bf16 products (bf16 / 4)
-            "roofline": {"bound": "tensor", "kernel": f"GEMM {M}x{N}x{K} ({path})",
-                         "achieved": tflops, "peak": bf16, "unit": "TFLOP/s",
-                         "frac": tflops / bf16, "peak_source": f"{src} bf16 dense (burst)",
-                         # captured for the one-GPU launch (65536 rows) only
-                         "traffic": GEMM_TRAFFIC_BYTES.get(args.gemm_scheme) if M == B_GLOBAL else None,
-                         "scheme_ceiling": ceiling,
-                         "frac_of_scheme_ceiling": tflops / ceiling,
-                         "launch": gemm_plan},
+            "roofline": roof,
             "e2e": {"value": 1000.0 / max(all_e2e), "unit": "steps/s",
                     "h2d_bytes_per_step": int(xs.nbytes + ts.nbytes) * world,
                     "d2h_bytes_per_step": 4 * world},
@@ -398,10 +614,8 @@ def run_ours(args, rank, world, local):
             "clocks": clk,
             "cpu_baseline": cpu,
         }
-        if fused is not None:
-            line["fused_op"] = fused
+        line.update(extra)
         print(json.dumps(line), flush=True)
-    P.free()
     comm.destroy()
     rdv.close()
     return 0
@@ -494,9 +708,12 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--cpu-rows", type=int, default=4096)
-    ap.add_argument("--no-cpu", action="store_true")
-    ap.add_argument("--no-fused", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true", help="no CPU baseline step")
+    ap.add_argument("--no-configs", action="store_true",
+                    help="one GPU: skip the split-TF32 step and the other workloads")
+    ap.add_argument("--no-cpu-configs", action="store_true",
+                    help="--impl reference: skip the other workloads")
+    ap.add_argument("--no-check", action="store_true", help="skip the GEMM error check")
     ap.add_argument("--gemm-m", type=int, default=8192, help="rows of the --micro gemm product")
     ap.add_argument("--gemm-scheme", choices=sorted(GEMM_SCHEMES), default="bf16x3",
                     help="tensor-core operand scheme of the fp32 GEMMs")

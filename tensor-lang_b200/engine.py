@@ -453,13 +453,21 @@ class Program:
         for s in self._all_steps():
             for r in s.reads:
                 read_count[r] = read_count.get(r, 0) + 1
-        for s in self.phase_pre:
-            if isinstance(s, _Loop):
-                live.update(s.writes)  # values visible after the loop
+        # a rebound value lives on in its target's buffer (the in-place
+        # update of a parameter); any other value a loop writes is kept only
+        # if some step reads it, or the caller fetches or saves it
+        live |= set(self.alias)
         self.live = live
+
+        def dead_zero(st) -> bool:
+            # a gradient that receives nothing is zero-filled (autograd.py:151-153);
+            # when nothing reads or keeps it, the fill is skipped
+            return isinstance(st, Memset0) and st.name not in live and \
+                read_count.get(st.name, 0) == 0
 
         def fz(lst, label):
             res, chunk = [], []
+            lst = [st for st in lst if not dead_zero(st)]
 
             def flush():
                 if not chunk:
@@ -577,9 +585,15 @@ class Program:
         gradients of a top-level backward, as the reference caches them)."""
         self.execute()
         self.sync()
-        names = self.fetch if self.fetch is not None else \
-            [n for n in self.buffers if not n.startswith("__")] + \
-            [a for a in self.alias if not a.startswith("__")]
+        if self.fetch is not None:
+            names = self.fetch
+        else:
+            # every value the program names (the frontend's own temporaries,
+            # such as inlined function results, included), none of the
+            # backend's internal buffers
+            lets = self._let_names()
+            names = [n for n in self.buffers if not n.startswith("__") or n in lets] + \
+                [a for a in self.alias if not a.startswith("__") or a in lets]
         out = {}
         for n in names:
             base = self.alias.get(n, n)
@@ -598,6 +612,18 @@ class Program:
                     p = self.save_dir / p
                 p.parent.mkdir(parents=True, exist_ok=True)
                 np.save(p, self.read(sv["tensor"]))
+        return out
+
+    def _let_names(self) -> set:
+        out = set()
+
+        def walk(nodes):
+            for n in nodes:
+                if n.get("type") == "for":
+                    walk(n["body"])
+                elif n.get("type") == "let":
+                    out.add(n["name"])
+        walk(self.ast)
         return out
 
     def arena_span(self):
