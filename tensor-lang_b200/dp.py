@@ -350,6 +350,22 @@ def loss_divisors(ast: list, shapes: Dict[str, Shape], derived: set) -> dict:
     return out
 
 
+def _batch_dependent(grad: str, bw: List[Step]) -> bool:
+    """Whether a replicated tensor's gradient can differ between ranks: some
+    backward step writes it from data.  Gradients that are only zero-filled
+    (tracked values the loss does not depend on, such as a rebound
+    ``W_new``) or only set to a constant (the loss seed, autograd.py:160) are
+    the same on every rank and are not all-reduced."""
+    from .steps import EW, Memset0
+    for st in bw:
+        if grad not in st.writes or isinstance(st, Memset0):
+            continue
+        if isinstance(st, EW) and all(o[0] == "const" for o in st.operands):
+            continue
+        return True
+    return False
+
+
 class DataParallelProgram:
     """A Program whose batch axis is split over ``comm.world`` GPUs."""
 
@@ -367,6 +383,7 @@ class DataParallelProgram:
 
         def hook(prog, exposed, bw):
             names = [f"{n}_grad" for n in exposed if n not in self.derived]
+            names = [n for n in names if _batch_dependent(n, bw)]
             self.replicated_grads = names
             prog.arena_names = list(names)
             if comm.world == 1 or not names:

@@ -176,3 +176,28 @@ def test_bucket_plan_overlaps_backward():
                 continue
             assert not (set(b.names) & (set(s.reads) | set(s.writes))), (b.label, s.label)
     assert sum(4 * numel(P.shapes[n]) for n in first.names) >= dp.BUCKET_BYTES
+
+
+def test_only_parameter_gradients_are_all_reduced():
+    """The gradient arena of the training loop holds exactly the six parameter
+    gradients, 21,020,682 floats (84 MB): the zero-filled gradients of the
+    rebound W_new / b_new values and the loss seed are the same on every rank
+    and are neither packed nor all-reduced."""
+    tl = load_backend()
+    from tensor_lang_b200 import dp
+    from tensor_lang_b200.shapes import numel
+    pr = tl.programs
+
+    class _Comm:
+        world, rank, handle, stream = 2, 0, None, None
+    kw = dict(B=512, I=1024, H=4096, C=10)
+    ast = pr.mlp3_train(epochs=1, **kw)
+    D = dp.DataParallelProgram(ast, None, _Comm(), device=0,
+                               feeds=pr.mlp3_inputs(rows=(0, 256), **kw), fetch=["loss", "W3"])
+    P = D.program
+    assert sorted(D.replicated_grads) == sorted(
+        ["W1_grad", "b1_grad", "W2_grad", "b2_grad", "W3_grad", "b3_grad"])
+    assert sum(numel(P.shapes[n]) for n in P.arena_names) == 21_020_682
+    P._fuse_all()
+    ar = [s for s in P._all_steps() if isinstance(s, dp.AllReduceBucket)]
+    assert len(ar) == 1 and sorted(ar[0].names) == sorted(D.replicated_grads)
