@@ -63,6 +63,14 @@ def set_gemm_scheme(tl, name):
     tl.runtime.check(tl.runtime.lib().tl_gemm_set_scheme(GEMM_SCHEMES[name][0], None), "gemm scheme")
 
 
+TILE_SCHEDULES = {"static": 0, "dynamic": 1, "auto": 2}
+
+
+def set_tile_schedule(tl, name):
+    tl.runtime.check(tl.runtime.lib().tl_gemm_set_tile_schedule(TILE_SCHEDULES[name], None),
+                     "tile schedule")
+
+
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -394,7 +402,8 @@ def hidden_gemm(tl, P, M, scheme, check: bool):
            "traffic": GEMM_TRAFFIC_BYTES.get(scheme) if M == B_GLOBAL else None,
            "scheme_ceiling": ceiling, "frac_of_scheme_ceiling": tflops / ceiling,
            "ms_per_call": ms,
-           "launch": {"k_splits": plan[1], "tiles_per_cluster": plan[2], "clusters": plan[3]}}
+           "launch": {"k_splits": plan[1], "tiles_per_cluster": plan[2], "clusters": plan[3],
+                      "schedule": {0: "single CTA", 1: "static", 2: "dynamic"}[plan[0]]}}
     if check:
         a1, C = P.read("a1"), P.read("a2")
         W2, b2 = P.read("W2").astype(np.float64), P.read("b2").astype(np.float64)
@@ -534,6 +543,7 @@ def run_ours(args, rank, world, local):
     tl = load_package()
     rt = tl.runtime
     set_gemm_scheme(tl, args.gemm_scheme)
+    set_tile_schedule(tl, args.tile_schedule)
     from tensor_lang_b200 import dp
 
     dev = local
@@ -639,6 +649,7 @@ def run_micro(args):
     dev = rt.Device.get(0)
     st = dev.stream
     set_gemm_scheme(tl, args.gemm_scheme)
+    set_tile_schedule(tl, args.tile_schedule)
     hbm, bf16, _, src = peaks()
     reps = args.steps
     if args.micro == "reductions":
@@ -662,7 +673,7 @@ def run_micro(args):
         P.free()
         return 0
     if args.micro == "gemm":
-        M, N, K = args.gemm_m, 4096, 4096
+        M, N, K = args.gemm_m, 4096, args.gemm_k
         rng = np.random.default_rng(0)
         A = rt.DeviceBuffer(dev, (M, K))
         A.upload(rng.standard_normal((M, K), dtype=np.float32))
@@ -703,6 +714,7 @@ def run_micro(args):
 
 
 def main():
+    global B_GLOBAL, METRIC
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -715,12 +727,23 @@ def main():
                     help="--impl reference: skip the other workloads")
     ap.add_argument("--no-check", action="store_true", help="skip the GEMM error check")
     ap.add_argument("--gemm-m", type=int, default=8192, help="rows of the --micro gemm product")
+    ap.add_argument("--gemm-k", type=int, default=4096, help="depth of the --micro gemm product")
+    ap.add_argument("--global-batch", type=int, default=B_GLOBAL,
+                    help="profiling aid: another global batch (8192 at one GPU is the per-rank "
+                         "work of eight)")
     ap.add_argument("--gemm-scheme", choices=sorted(GEMM_SCHEMES), default="bf16x3",
                     help="tensor-core operand scheme of the fp32 GEMMs")
+    ap.add_argument("--tile-schedule", choices=sorted(TILE_SCHEDULES), default="auto",
+                    help="CTA-pair GEMM tile schedule: static groups, dynamic (running "
+                         "clusters take pending clusters' tiles), or auto (the library's choice "
+                         "per launch)")
     ap.add_argument("--micro", choices=["gemm", "fused", "softmax", "rowsum", "reductions"],
                     default=None,
                     help="time one kernel alone (profiling aid); prints its own JSON line")
     args = ap.parse_args()
+    if args.global_batch != B_GLOBAL:
+        B_GLOBAL = args.global_batch
+        METRIC = METRIC.replace("batch 65536", f"batch {B_GLOBAL}")
     if args.micro:
         return run_micro(args)
     rank, world, local = dist_env()

@@ -274,9 +274,10 @@ int  tl_gemm_path(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                   const float* A, int64_t lda, const float* B, int64_t ldb,
                   const float* C, int64_t ldc);
 /* The tensor-core launch for an M x N x K product (no reference
- * counterpart; host-only, no GPU needed): plan[0] 1 for 256 x 256 CTA-pair
- * tiles, 0 for 128 x 256 single-CTA tiles; plan[1] K splits; plan[2] tiles
- * each CTA pair computes in turn; plan[3] clusters (CTA pairs) or CTAs
+ * counterpart; host-only, no GPU needed): plan[0] 0 for 128 x 256 single-CTA
+ * tiles, 1 for 256 x 256 CTA-pair tiles on the static schedule, 2 on the
+ * dynamic one (tl_gemm_set_tile_schedule); plan[1] K splits; plan[2] tiles
+ * each cluster launch starts with; plan[3] clusters (CTA pairs) or CTAs
  * launched.  Uses this device's SM count (148 when no GPU is visible). */
 int  tl_gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* plan);
 /* Path selection: 0 automatic (tensor cores when the shape allows, the raw
@@ -309,6 +310,20 @@ int  tl_gemm_set_scheme(int scheme, int* previous);
  * of B; enable = 0: 128 x 256 single-CTA tiles only.  *previous (if non-null)
  * receives the setting that was in force. */
 int  tl_gemm_set_cta_pair(int enable, int* previous);
+/* Tile schedule of the 256 x 256 CTA-pair kernel (no reference
+ * counterpart).  dynamic = 0: static groups -- each cluster launch computes
+ * up to four consecutive tiles in turn on launches of many waves, one tile
+ * otherwise, and the hardware balances the cluster launches; dynamic = 1:
+ * one tile per cluster launch, and each running cluster goes on with the
+ * tiles of clusters that have not started (sm_100 cluster launch control:
+ * the launch of a pending cluster is cancelled and its tile computed by the
+ * running one), so an SM pair computes tiles back to back, its stage ring
+ * and accumulators running on, until none are left; dynamic = 2 (default):
+ * dynamic for launches the static schedule leaves at one tile per cluster
+ * and for K <= 1024, static otherwise.  Results are bit-identical under
+ * every schedule.  *previous (if non-null) receives the setting that was in
+ * force. */
+int  tl_gemm_set_tile_schedule(int dynamic, int* previous);
 /* Device-side error flag (TL_ERR_TIMEOUT after a bounded wait in a kernel
  * gave up; 0 if none).  reset != 0 clears it. */
 int  tl_device_error(int* code, int reset);

@@ -275,6 +275,7 @@ struct Params {
   int splits;         // CTA-pair kernel: K split this many ways (1: no split)
   float* partial;     // [splits][M][N] raw sums when splits > 1
   int tpc = 1;        // CTA-pair kernel: tiles each cluster computes in turn
+  int clc = 0;        // CTA-pair kernel: take pending clusters' tiles (cluster launch control)
 };
 
 // Split-K partial of one thread's BN/2 columns of row `row` (no epilogue).
@@ -588,7 +589,7 @@ constexpr int STAGES2 = 3;
 constexpr int HB = 128;                            // B rows (N) held per CTA
 constexpr int B_HALF = HB * BK * 4;                // 16 KB
 constexpr int STAGE2_BYTES = 2 * A_TILE + 2 * B_HALF;  // 64 KB per CTA
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 256;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 512;
 // The BF16X3 scheme stages only the two pair tiles (32 KB per CTA), so twice
 // as many stages fit in the same shared memory.
 template <int SCHEME>
@@ -671,6 +672,49 @@ __device__ __forceinline__ void mma2_commit_both(uint32_t bar) {
       : "memory");
 }
 
+// Dynamic tile scheduling with cluster launch control (sm_100): one thread
+// asks the hardware to cancel the launch of a cluster that has not started
+// yet; the 16-byte answer is written to the same shared-memory offset in
+// both CTAs of the pair and completes each CTA's mbarrier there.  When the
+// cancel succeeded, this cluster computes the cancelled cluster's tiles.
+constexpr int CLC_SLOTS = 4;  // answers in flight before one must be consumed
+__device__ __forceinline__ void clc_try_cancel(uint32_t resp, uint32_t bar) {
+  asm volatile(
+      "clusterlaunchcontrol.try_cancel.async.shared::cta.mbarrier::complete_tx::bytes"
+      ".multicast::cluster::all.b128 [%0], [%1];" ::"r"(resp),
+      "r"(bar)
+      : "memory");
+}
+// blockIdx.x of the first CTA of the cancelled cluster, or -1 when the
+// answer says no cluster was left to cancel
+__device__ __forceinline__ int clc_first_ctaid_x(uint32_t resp) {
+  int x;
+  asm volatile(
+      "{\n\t.reg .b128 r;\n\t.reg .pred p;\n\t"
+      "ld.shared.b128 r, [%1];\n\t"
+      "clusterlaunchcontrol.query_cancel.is_canceled.pred.b128 p, r;\n\t"
+      "mov.s32 %0, -1;\n\t"
+      "@p clusterlaunchcontrol.query_cancel.get_first_ctaid::x.b32.b128 %0, r;\n\t}"
+      : "=r"(x)
+      : "r"(resp)
+      : "memory");
+  return x;
+}
+
+// Answer r (the group after a cluster's r-th group): wait for it in this
+// CTA, read it and (arrive) tell the leader's clc_empty it was read.  Returns
+// the next group, -1 when no cluster was left to cancel, -2 when the wait
+// gave up.
+__device__ __forceinline__ int clc_next_group(int r, uint64_t* clc_full, bool arrive) {
+  const uint32_t q = (uint32_t)(r % CLC_SLOTS);
+  const uint32_t full0 = smem_u32(clc_full);
+  if (!mbar_wait(full0 + 8u * q, (uint32_t)(r / CLC_SLOTS) & 1u)) return -2;
+  // layout: clc_full[CLC_SLOTS], clc_empty[CLC_SLOTS], answers[CLC_SLOTS][16 B]
+  const int x = clc_first_ctaid_x(full0 + 16u * CLC_SLOTS + 16u * q);
+  if (arrive) mbar_arrive_cluster(mapa_shared(full0 + 8u * CLC_SLOTS, 0) + 8u * q);
+  return x < 0 ? -1 : (x >> 1);
+}
+
 template <int A_MN, int B_MN>
 __host__ __device__ constexpr uint32_t idesc2_tf32() {
   return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)A_MN << 15) | ((uint32_t)B_MN << 16) |
@@ -697,17 +741,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   uint64_t* empty = bars + NST;         // [NST] MMA -> each CTA's producer
   uint64_t* acc_full = bars + 2 * NST;  // [2] MMA -> each CTA's epilogue
   uint64_t* acc_free = acc_full + 2;        // [2] both CTAs' epilogues -> leader's MMA
-  uint32_t* tmem_slot = (uint32_t*)(acc_free + 2);
+  uint64_t* clc_full = acc_free + 2;        // [CLC_SLOTS] scheduling answer arrived (each CTA)
+  uint64_t* clc_empty = clc_full + CLC_SLOTS;  // [CLC_SLOTS] answer read by every role (leader)
+  unsigned char* clc_resp = (unsigned char*)(clc_empty + CLC_SLOTS);  // [CLC_SLOTS][16 B]
+  uint32_t* tmem_slot = (uint32_t*)(clc_resp + 16 * CLC_SLOTS);
 
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // This cluster's tiles: global indices g0 .. g0 + ntl - 1 (tile2_of).
+  // Tiles come in groups of p.tpc consecutive global indices (tile2_of): group
+  // c is cluster c's launch; this cluster starts with its own group and, with
+  // p.clc, goes on with the groups of the clusters it cancels.
   const int n_tiles = (p.N + 255) / 256, m_tiles = (p.M + 255) / 256;
   const int nk_all = (p.K + BK - 1) / BK;
+  const int total = p.splits * m_tiles * n_tiles;
   const int cid = (int)(blockIdx.x >> 1);
-  const int g0 = cid * p.tpc;  // this cluster's first tile
-  const int ntl = min(p.tpc, p.splits * m_tiles * n_tiles - g0);
+  // every role that reads a scheduling answer arrives once on the leader's
+  // clc_empty: both producers, the MMA thread, both CTAs' epilogue warps
+  constexpr uint32_t kClcReaders = 3 + 2 * EPI_WARPS;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
@@ -717,6 +768,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&acc_full[b]), 1);
       mbar_init(smem_u32(&acc_free[b]), 2 * EPI_WARPS);
+    }
+    for (int q = 0; q < CLC_SLOTS; ++q) {
+      mbar_init(smem_u32(&clc_full[q]), 1);
+      mbar_init(smem_u32(&clc_empty[q]), kClcReaders);
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -732,7 +787,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   cluster_sync_all();
   fence_after();
   const uint32_t tmem = *tmem_slot;
-
   // The stage ring and the two accumulators run on across the cluster's
   // tiles: k-block `it` (counted over all its tiles) uses stage it % NST,
   // chunk `cg` accumulator cg & 1, so the loads and MMAs of the next tile
@@ -743,6 +797,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the leader's full[0]
       bool ok = true;
       int it = 0;
+      for (int grp = cid, r = 0; ok; ++r) {
+      const int g0 = grp * p.tpc, ntl = min(p.tpc, total - g0);
       for (int t = 0; t < ntl && ok; ++t) {
         const Tile2 tt = tile2_of(p, g0 + t, m_tiles, n_tiles, nk_all);
         const int m0 = tt.m0 + 128 * (int)rank;  // this CTA's rows of A
@@ -804,6 +860,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
         }
       }
+      if (!ok || !p.clc) break;
+      // every load of this group is issued: ask for the next group (the
+      // leader), expect this CTA's copy of the answer, then read it
+      {
+        const int q = r % CLC_SLOTS;
+        mbar_expect_tx(smem_u32(&clc_full[q]), 16);
+        if (leader) {
+          if (r >= CLC_SLOTS &&
+              !mbar_wait(smem_u32(&clc_empty[q]), (uint32_t)(r / CLC_SLOTS - 1) & 1u)) {
+            ok = false;
+            break;
+          }
+          clc_try_cancel(smem_u32(clc_resp + 16 * q), smem_u32(&clc_full[q]));
+        }
+      }
+      grp = clc_next_group(r, clc_full, true);
+      if (grp < 0) break;
+      }
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -812,6 +886,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       constexpr uint32_t idesc = idesc2_tf32<TA, TB ? 0 : 1>();
       bool ok = true;
       int it = 0, cg = 0;
+      for (int grp = cid, r = 0; ok; ++r) {
+      const int g0 = grp * p.tpc, ntl = min(p.tpc, total - g0);
       for (int t = 0; t < ntl && ok; ++t) {
         const Tile2 tt = tile2_of(p, g0 + t, m_tiles, n_tiles, nk_all);
         const int nchunks = (tt.nk + KC - 1) / KC;
@@ -878,6 +954,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           mma2_commit_both(smem_u32(&acc_full[b]));  // chunk ready in both CTAs
         }
       }
+      if (!ok || !p.clc) break;
+      grp = clc_next_group(r, clc_full, true);
+      if (grp < 0) break;
+      }
     }
     __syncwarp();
   } else {
@@ -891,6 +971,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     float sum[BN / 2];
     bool ok = true;
     int cg = 0;
+    for (int grp = cid, r = 0; ok; ++r) {
+    const int g0 = grp * p.tpc, ntl = min(p.tpc, total - g0);
     for (int g = g0; g < g0 + ntl && ok; ++g) {
       // only the chunk count is needed while the tile drains (the registers
       // hold the row's partial sums); its position is derived for the store
@@ -935,6 +1017,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         else
           store_row(p, row, tt.n0 + half * (BN / 2), sum);
       }
+    }
+    if (!ok || !p.clc) break;
+    // every lane reads the answer; lane 0 reports the warp's read
+    grp = clc_next_group(r, clc_full, lane == 0);
+    __syncwarp();
+    if (grp < 0) break;
     }
   }
   fence_before();
@@ -1253,6 +1341,12 @@ int g_split_mode = 0;  // 0: raw operand is hi (lo pre-pass); 1: hi and lo both 
 int g_scheme = kSchemeBF16X3;
 int g_cta_pair = 1;  // 256 x 256 CTA-pair tiles when the product has more than one row tile
 int g_tiles_per_cluster = 4;  // upper bound on the tiles one CTA pair computes in turn
+// CTA-pair tile schedule: 0 static groups of tiles_per_cluster tiles, one per
+// cluster launch; 1 dynamic: one tile per cluster launch, and every running
+// cluster takes the tiles of clusters not launched yet (cluster launch
+// control), so an SM pair computes tiles back to back until none are left;
+// 2 (default) dynamic where it measured faster (use_dynamic)
+int g_tile_dynamic = 2;
 
 // Tiles per cluster for a CTA-pair launch of `tiles` tiles: each cluster
 // launch pays a prologue (barrier set-up, TMEM allocation, pipeline fill) and
@@ -1274,6 +1368,15 @@ int tiles_per_cluster(int64_t tiles) {
     if (clusters >= 4 * slots && eff(clusters) >= base - 0.01) return t;
   }
   return 1;
+}
+
+// The automatic schedule.  Measured on one B200 (BF16X3, CUDA events):
+// dynamic against static 65536x4096x1024 +6%, 8192x4096x1024 +18%,
+// 8192x4096x4096 +2.4% (launches static leaves at one tile per cluster, or
+// with short tiles), 65536x4096x4096 -0.5% (four tiles per cluster already).
+bool use_dynamic(int64_t work, int64_t K) {
+  if (g_tile_dynamic != 2) return g_tile_dynamic == 1;
+  return tiles_per_cluster(work) == 1 || K <= 1024;
 }
 
 // K splits for the CTA-pair kernel: a product of only a few waves of cluster
@@ -1305,7 +1408,8 @@ int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CU
     if (2 * clusters * splits > INT32_MAX) return TL_ERR_UNSUPPORTED;
     Params q = p;
     q.splits = splits;
-    q.tpc = tiles_per_cluster(clusters * splits);
+    q.clc = use_dynamic(clusters * splits, p.K) ? 1 : 0;
+    q.tpc = q.clc ? 1 : tiles_per_cluster(clusters * splits);
     const int64_t launched = (clusters * splits + q.tpc - 1) / q.tpc;  // clusters launched
     if (splits > 1) {
       float* part = nullptr;
@@ -1516,8 +1620,9 @@ int gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* out) {
   const int64_t clusters = ((M + 255) / 256) * ((N + 255) / 256);
   const int splits = split_count(clusters, (K + BK - 1) / BK);
   if (2 * clusters * splits > INT32_MAX) return TL_ERR_UNSUPPORTED;
-  const int tpc = tiles_per_cluster(clusters * splits);
-  out[0] = 1;
+  const bool dyn = use_dynamic(clusters * splits, K);
+  const int tpc = dyn ? 1 : tiles_per_cluster(clusters * splits);
+  out[0] = dyn ? 2 : 1;
   out[1] = splits;
   out[2] = tpc;
   out[3] = (int)((clusters * splits + tpc - 1) / tpc);
@@ -1529,6 +1634,12 @@ void gemm_set_split_mode(int mode) { g_split_mode = mode; }
 int gemm_set_cta_pair(int enable) {
   const int prev = g_cta_pair;
   g_cta_pair = enable ? 1 : 0;
+  return prev;
+}
+
+int gemm_set_tile_dynamic(int mode) {
+  const int prev = g_tile_dynamic;
+  g_tile_dynamic = mode;
   return prev;
 }
 

@@ -122,6 +122,7 @@ _SIGS = [
     ("tl_gemm_force_simt", c_int, [c_int]),
     ("tl_gemm_set_scheme", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_gemm_set_cta_pair", c_int, [c_int, ctypes.POINTER(c_int)]),
+    ("tl_gemm_set_tile_schedule", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_device_error", c_int, [ctypes.POINTER(c_int), c_int]),
     ("tl_nccl_unique_id", c_int, [ctypes.c_char_p]),
     ("tl_nccl_comm_init", c_int, [ctypes.POINTER(c_void_p), c_int, ctypes.c_char_p, c_int, c_int]),

@@ -7,7 +7,9 @@ Rules under test (csrc/gemm_tc.cu): a launch of few cluster waves splits K
 until the waves are >= 95% full, keeping >= 8 k-blocks per split; a launch of
 many waves lets each CTA pair compute up to four tiles in turn while at least
 four waves of clusters remain and the last wave is no emptier (within 1%)
-than with one tile per cluster."""
+than with one tile per cluster.  The automatic tile schedule is dynamic
+(running CTA pairs take pending clusters' tiles) where that would leave one
+tile per cluster, and for K <= 1024."""
 import ctypes
 import math
 
@@ -27,10 +29,10 @@ def _plan(M, N, K):
 
 @pytest.mark.parametrize("M,N,K,plan", [
     (65536, 4096, 4096, (1, 1, 4, 1024)),   # hidden forward / dX: four tiles per pair
-    (65536, 4096, 1024, (1, 1, 4, 1024)),   # first layer
-    (4096, 4096, 65536, (1, 2, 1, 512)),    # dW2: 256 tiles, K split in two
-    (1024, 4096, 65536, (1, 8, 1, 512)),    # dW1: 64 tiles, K split eight ways
-    (8192, 4096, 4096, (1, 1, 1, 512)),     # the 8-GPU per-rank forward: 6.9 waves
+    (65536, 4096, 1024, (2, 1, 1, 4096)),   # first layer: short tiles, dynamic schedule
+    (4096, 4096, 65536, (2, 2, 1, 512)),    # dW2: 256 tiles, K split in two, dynamic
+    (1024, 4096, 65536, (2, 8, 1, 512)),    # dW1: 64 tiles, K split eight ways, dynamic
+    (8192, 4096, 4096, (2, 1, 1, 512)),     # the 8-GPU per-rank forward: 6.9 waves, dynamic
     (64, 256, 256, (0, 1, 1, 1)),           # one row tile: single-CTA 128 x 256
 ])
 def test_training_step_plans(M, N, K, plan):
@@ -46,7 +48,10 @@ def _eff(clusters):
 @pytest.mark.parametrize("K", [32, 520, 4096, 65536])
 def test_plan_invariants(M, N, K):
     pair, splits, tpc, launched = _plan(M, N, K)
-    assert pair == 1
+    assert pair in (1, 2)
+    # the automatic schedule: dynamic where static would leave one tile per
+    # cluster, and for short tiles
+    assert (pair == 2) == (tpc == 1 or K <= 1024) and (pair == 1 or tpc == 1)
     tiles = math.ceil(M / 256) * math.ceil(N / 256)
     work = tiles * splits
     nk = math.ceil(K / 32)
@@ -76,3 +81,20 @@ def test_plan_rejects_empty_products():
     out = (ctypes.c_int * 4)()
     assert L.tl_gemm_tc_plan(0, 4096, 4096, out) != 0
     assert L.tl_gemm_tc_plan(64, 4096, 0, out) != 0
+
+
+@pytest.mark.parametrize("M,N,K,plan", [
+    (65536, 4096, 4096, (2, 1, 1, 4096)),   # one tile per cluster launch
+    (4096, 4096, 65536, (2, 2, 1, 512)),    # the K splits are unchanged
+    (8192, 4096, 4096, (2, 1, 1, 512)),
+])
+def test_plan_under_the_dynamic_schedule(M, N, K, plan):
+    L = load_backend().runtime.lib()
+    prev = ctypes.c_int(-1)
+    assert L.tl_gemm_set_tile_schedule(1, ctypes.byref(prev)) == 0
+    try:
+        assert _plan(M, N, K) == plan
+    finally:
+        L.tl_gemm_set_tile_schedule(prev.value, None)
+    assert prev.value == 2
+    assert L.tl_gemm_set_tile_schedule(3, None) != 0

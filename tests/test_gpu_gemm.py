@@ -247,3 +247,54 @@ def _prepared_pairs_case(ta, tb, M, N, K):
     ref = (A.astype(np.float64).T if ta else A.astype(np.float64)) @ \
         (B.astype(np.float64).T if tb else B.astype(np.float64))
     assert_close(c2, ref, 1e-5, f"prepared pairs {ta}{tb} {M}x{N}x{K}")
+
+
+class _Schedule:
+    """Select the CTA-pair tile schedule for the duration of a with-block."""
+
+    def __init__(self, dynamic):
+        self.dynamic = dynamic
+
+    def __enter__(self):
+        tl = load_backend()
+        self.L = tl.runtime.lib()
+        self.prev = ctypes.c_int(-1)
+        tl.runtime.check(self.L.tl_gemm_set_tile_schedule(self.dynamic, ctypes.byref(self.prev)))
+        return self
+
+    def __exit__(self, *exc):
+        self.L.tl_gemm_set_tile_schedule(self.prev.value, None)
+        return False
+
+
+@pytest.mark.parametrize("scheme", [0, 1, 2])
+@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
+@pytest.mark.parametrize("M,N,K", [(200, 300, 100), (1024, 512, 512), (4096, 256, 4096),
+                                   (256, 128, 16384), (18900, 4056, 520)])
+def test_gemm_dynamic_tile_schedule(scheme, ta, tb, M, N, K):
+    """Dynamic tile scheduling (cluster launch control: running CTA pairs
+    take the tiles of clusters not launched yet) gives the static schedule's
+    product bit for bit -- each tile's arithmetic is the same wherever it
+    runs -- on ragged shapes, split K (256 x 128 x 16384) and launches of
+    many waves, under every operand scheme, and within rel 1e-5 of float64."""
+    with _Scheme(scheme):
+        with _Schedule(0):
+            static, ref, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
+        assert err == 0 and path == 0
+        with _Schedule(1):
+            dyn, _, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
+        assert err == 0 and path == 0
+    np.testing.assert_array_equal(dyn, static)
+    assert_close(dyn, ref, 1e-5, f"dynamic schedule {scheme} {ta}{tb} {M}x{N}x{K}")
+
+
+def test_gemm_dynamic_schedule_accumulate_and_plan():
+    tl = load_backend()
+    L = tl.runtime.lib()
+    with _Schedule(1):
+        out, ref, path, err = _run(0, 1, 2048, 1024, 768, bias=True, acc=True)
+        plan = (ctypes.c_int * 4)()
+        tl.runtime.check(L.tl_gemm_tc_plan(65536, 4096, 4096, plan))
+    assert err == 0 and path == 0
+    assert_close(out, ref, 1e-5, "dynamic schedule, accumulate")
+    assert plan[2] == 1 and plan[3] == 4096, "one tile per cluster launch"
