@@ -9,9 +9,10 @@ minutes of CPU; the fixture keeps what the comparison needs).
 What is compared, and why this way:
 
 * the loss of the last epoch: rel 1e-4;
-* the parameters after the run: rel 1e-4, atol 1e-4 * max|ref| (exactly for
-  the biases and the head, through the fixed projections ``P @ V`` for the
-  two large weights);
+* the weights after the run: rel 1e-4, atol 1e-4 * max|ref| (exactly for
+  the head, through the fixed projections ``W @ V`` for the two large
+  weights; the biases start at zero, so their final values are their
+  updates, compared next);
 * each parameter's update ``D = P_final - P_initial`` (the parameters
   themselves hide it: the update is ~1e-3 of ``P``), in relative Frobenius
   norm ``||D_gpu - D_ref|| / ||D_ref||``, exactly for the biases and the
@@ -86,8 +87,10 @@ def test_training_run_matches_the_float64_oracle(run, scheme):
             err = np.linalg.norm(D - fx[f"{run}/{p}/delta"])
             ref = feeds[p].astype(np.float64) + fx[f"{run}/{p}/delta"]
             got = out[p].astype(np.float64)
-        # the parameters themselves (projected for the large weights): rel 1e-4
-        assert_close(got, ref, 1e-4, f"{run} {p}")
+        # the weights themselves (projected for the large ones): rel 1e-4; a
+        # bias starts at zero, so its final value is its update, checked below
+        if p.startswith("W"):
+            assert_close(got, ref, 1e-4, f"{run} {p}")
         dev = err / norm
         dev32 = float(fx[f"{run}/{p}/dev32"])
         print(f"{run} scheme {scheme} {p}: update deviation {dev:.2e} (float32 oracle {dev32:.2e})")
