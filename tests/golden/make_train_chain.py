@@ -26,10 +26,11 @@ parameter ``P`` with update ``D = P_final - P_initial``:
   float32 oracle's update is from the float64 one (exact, not projected);
 * ``<run>/loss64``, ``<run>/loss32`` -- the loss of the last epoch.
 
-The float32 deviation is the scale of the GPU test's bound: a relu whose
+The float32 deviation is printed beside the GPU's by the test: a relu whose
 pre-activation sits within rounding distance of 0 can take either branch in
 any float32 evaluation, and one such flip moves a whole row or column of a
-weight gradient (see ``tests/test_gpu_full_size.py``).
+weight gradient, so no float32 run matches a float64 update elementwise
+(see ``tests/test_gpu_train_chain.py``).
 """
 from __future__ import annotations
 

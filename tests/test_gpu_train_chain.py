@@ -22,12 +22,14 @@ What is compared, and why this way:
   0 takes either branch, and one such flip moves a whole row of ``h1_grad``
   into every column of ``W1_grad`` and a whole entry into ``b1_grad``.  The
   fixture records how far the float32 oracle -- the reference's own
-  arithmetic -- lands from float64 on the same run (``dev32``).  The number
-  of flips grows with the error of the products that feed each relu, about
-  5e-6 of max|C| for the default BF16X3 GEMMs against about 4e-7 for
-  float32 NumPy, so the GPU's update may land up to 10x farther (plus 1e-4);
-  the run is repeated with the split-TF32 GEMMs (about 2e-6).  Each kernel
-  on this path is held to rel 1e-4 (GEMMs) or 1e-5 from its own inputs at
+  arithmetic -- lands from float64 on the same run (``dev32``, printed
+  beside each GPU figure): up to 4.2e-3 (``W1`` after 3 full-batch epochs).
+  Flips make the deviation chaotic rather than proportional to the
+  products' error (the split-TF32 GEMMs, more accurate than BF16X3, moved
+  ``b1`` farther over 100 epochs), so the bound is absolute: 1e-2 of the
+  update's norm.  A wiring error in the loop (a stale operand, a lost
+  update, a wrong divisor) moves an update by O(1).  Each kernel on this
+  path is held to rel 1e-4 (GEMMs) or 1e-5 from its own inputs at
   these sizes in ``tests/test_gpu_full_size.py``.
 """
 import importlib.util
@@ -94,6 +96,6 @@ def test_training_run_matches_the_float64_oracle(run, scheme):
         dev = err / norm
         dev32 = float(fx[f"{run}/{p}/dev32"])
         print(f"{run} scheme {scheme} {p}: update deviation {dev:.2e} (float32 oracle {dev32:.2e})")
-        if dev > 10 * dev32 + 1e-4:
-            bad.append(f"{p}: {dev:.3e} vs float32 oracle {dev32:.3e}")
+        if dev > 1e-2:
+            bad.append(f"{p}: {dev:.3e} (float32 oracle {dev32:.3e})")
     assert not bad, f"{run}: " + "; ".join(bad)
