@@ -575,7 +575,9 @@ def run_ours(args, rank, world, local):
     # e2e through the public API: every step's batch comes from pinned host
     # memory and every step's loss goes back to the host
     xs, ts = feeds["x"], feeds["t"]
-    e2e_steps = max(1, min(args.steps, 10))
+    # as many steps as the device-timed region: the first batch's upload is
+    # the one that overlaps nothing
+    e2e_steps = max(1, args.steps)
     e2e_ms = e2e_time(tl, rt.Device.get(dev), loop, stream, P.ptr("x"), P.ptr("t"), P.ptr("loss"),
                       xs, ts, e2e_steps)
     rdv.barrier()
