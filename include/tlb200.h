@@ -324,6 +324,31 @@ int  tl_gemm_set_cta_pair(int enable, int* previous);
  * every schedule.  *previous (if non-null) receives the setting that was in
  * force. */
 int  tl_gemm_set_tile_schedule(int dynamic, int* previous);
+/* ---- classifier head of a training step, fused ---------------------------
+ * linear (kernel_generator.py:1584-1661) with N <= 16 outputs, row softmax
+ * (:564-640) and cross_entropy (:1816-1885), and their backward:
+ * the cross_entropy VJP chained through the softmax VJP (autograd.py:691-704,
+ * :563-580) and the linear VJP's dX (:619-646) with the relu-VJP mask of the
+ * layer below (autograd.py:540-544), in one pass over A [M, K]:
+ *   z = A W + bias; p = softmax(z); dp = (p - t) / divisor * upstream[0];
+ *   dz = dp p - p sum(dp p); dx = (dz W^T) * (mask > 0).
+ * W is [K, N] with leading dimension ldw; target one-hot [M, N] (onehot 1)
+ * or class indices [M] (onehot 0); z, p, dp, dz ([M, N], leading dimension
+ * N) are written when non-null; dx [M, K] (leading dimension lddx) and mask
+ * [M, K] (leading dimension ldm) are required.  The results are
+ * bit-identical to tl_gemm + tl_softmax_rows + tl_ce_softmax_backward +
+ * tl_gemm_masked on the same operands; the loss itself is tl_cross_entropy's
+ * (it reads p).  tl_head_ce_ok tells whether a shape is supported (N <= 16,
+ * K a multiple of 4, 16-byte aligned A, dx and mask, lda, lddx and ldm
+ * multiples of 4, M * K >= 65536); other shapes return TL_ERR_UNSUPPORTED.
+ * No reference counterpart as one call. */
+int  tl_head_ce_ok(int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
+                   const float* dx, int64_t lddx);
+int  tl_head_ce(const float* A, int64_t lda, const float* W, int64_t ldw, const float* bias,
+                const float* target, int onehot, const float* upstream, float divisor,
+                float* z, float* p, float* dp, float* dz, float* dx, int64_t lddx,
+                const float* mask, int64_t ldm, int64_t M, int64_t N, int64_t K, void* stream);
+
 /* Device-side error flag (TL_ERR_TIMEOUT after a bounded wait in a kernel
  * gave up; 0 if none).  reset != 0 clears it. */
 int  tl_device_error(int* code, int reset);

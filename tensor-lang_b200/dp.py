@@ -372,7 +372,7 @@ class DataParallelProgram:
     def __init__(self, ast: list, env: Optional[dict], comm: Communicator, *, device: int,
                  feeds: Dict[str, np.ndarray], fetch: Optional[Sequence[str]] = None,
                  sharded: Sequence[str] = ("x", "t"), use_graphs: bool = True,
-                 bucket_bytes: Optional[int] = None):
+                 bucket_bytes: Optional[int] = None, fuse_head: bool = True):
         self.comm = comm
         gshapes = complete_env(ast, env or {})
         self.derived = batch_derived(ast, sharded)
@@ -393,7 +393,8 @@ class DataParallelProgram:
             return bw
 
         self.program = Program(ast, None, device=device, feeds=feeds, fetch=fetch, shapes=local,
-                               divisors=divisors, grad_hook=hook, use_graphs=use_graphs)
+                               divisors=divisors, grad_hook=hook, use_graphs=use_graphs,
+                               fuse_head=fuse_head)
 
     def run(self):
         return self.program.run()

@@ -30,6 +30,7 @@ from . import runtime as rt
 from .autograd import BackwardPlanner, Node, grad_name
 from .dataio import check_shape, load_data_file
 from .epilogue import fuse_gemm_epilogues
+from .head import fuse_classifier_head
 from .pairs import plan_gemm_pairs
 from .kernel_generator import KernelGenerator
 from .shapes import Shape, broadcast, complete_env, expr_inputs, numel
@@ -228,7 +229,8 @@ class Program:
     def __init__(self, ast: list, env: Optional[dict] = None, *, device: int = 0,
                  feeds: Optional[Dict[str, np.ndarray]] = None, fetch: Optional[Iterable[str]] = None,
                  load_files: Optional[Dict[str, np.ndarray]] = None, record: str = "extended",
-                 use_graphs: bool = True, fuse_ops: bool = True, save_dir: Optional[str] = None,
+                 use_graphs: bool = True, fuse_ops: bool = True, fuse_head: bool = True,
+                 save_dir: Optional[str] = None,
                  shapes: Optional[Dict[str, Shape]] = None, divisors: Optional[dict] = None,
                  grad_hook=None, semantics: str = "reference"):
         if semantics not in ("reference", "numpy"):
@@ -243,6 +245,7 @@ class Program:
         self.recorded = RECORDED_EXTENDED if record == "extended" else RECORDED_REFERENCE
         self.use_graphs = use_graphs
         self.fuse_ops = fuse_ops
+        self.fuse_head = fuse_head  # classifier-head fusion (head.py), with fuse_ops
         self.save_dir = Path(save_dir) if save_dir else Path.cwd()
         self.divisors = divisors or {}
         self.grad_hook = grad_hook  # (program, exposed grads, backward steps) -> backward steps
@@ -443,6 +446,8 @@ class Program:
     def _fuse_all(self):
         if self.fuse_ops:
             fuse_gemm_epilogues(self)
+            if self.fuse_head:
+                fuse_classifier_head(self)
             plan_gemm_pairs(self)
         live = set(self.shapes) if self.fetch is None else set(self.fetch)
         live |= set(self.initial)

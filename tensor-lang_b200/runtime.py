@@ -123,6 +123,10 @@ _SIGS = [
     ("tl_gemm_set_scheme", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_gemm_set_cta_pair", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_gemm_set_tile_schedule", c_int, [c_int, ctypes.POINTER(c_int)]),
+    ("tl_head_ce_ok", c_int, [c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
+    ("tl_head_ce", c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int,
+                           c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                           c_int64, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p]),
     ("tl_device_error", c_int, [ctypes.POINTER(c_int), c_int]),
     ("tl_nccl_unique_id", c_int, [ctypes.c_char_p]),
     ("tl_nccl_comm_init", c_int, [ctypes.POINTER(c_void_p), c_int, ctypes.c_char_p, c_int, c_int]),
