@@ -152,28 +152,47 @@ __global__ void __launch_bounds__(32 * kHeadWarps, 1)
     for (int r = 0; r < RPW; ++r)
 #pragma unroll
       for (int n = 0; n < NB; ++n) dzv[r][n] = __shfl_sync(0xffffffffu, dzl[r], n);
-    for (int q = lane; q < nq; q += 32) {
-      float4 w[NB];
+    // the mask vectors of U column steps are loaded before any of them is
+    // used, so U * RPW loads of 16 bytes are in flight a lane
+    constexpr int U = RPW <= 2 ? 4 : 2;
+    for (int q0 = lane; q0 < nq; q0 += 32 * U) {
+      float4 mk[U][RPW];
 #pragma unroll
-      for (int n = 0; n < NB; ++n) w[n] = *reinterpret_cast<const float4*>(&Wt[n * ldt + 4 * q]);
+      for (int u = 0; u < U; ++u)
 #pragma unroll
-      for (int r = 0; r < RPW; ++r) {
-        const int64_t m = m_base + r;
-        if (m >= M) break;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          v[0] = fmaf(dzv[r][n], w[n].x, v[0]);
-          v[1] = fmaf(dzv[r][n], w[n].y, v[1]);
-          v[2] = fmaf(dzv[r][n], w[n].z, v[2]);
-          v[3] = fmaf(dzv[r][n], w[n].w, v[3]);
+        for (int r = 0; r < RPW; ++r) {
+          const int q = q0 + 32 * u;
+          const int64_t m = m_base + r;
+          mk[u][r] = (q < nq && m < M)
+                         ? __ldg(reinterpret_cast<const float4*>(mask + m * ldm + 4 * q))
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        const float4 mk = __ldg(reinterpret_cast<const float4*>(mask + m * ldm + 4 * q));
-        v[0] = __fmul_rn(__fadd_rn(v[0], 0.f), mk.x > 0.f ? 1.f : 0.f);
-        v[1] = __fmul_rn(__fadd_rn(v[1], 0.f), mk.y > 0.f ? 1.f : 0.f);
-        v[2] = __fmul_rn(__fadd_rn(v[2], 0.f), mk.z > 0.f ? 1.f : 0.f);
-        v[3] = __fmul_rn(__fadd_rn(v[3], 0.f), mk.w > 0.f ? 1.f : 0.f);
-        *reinterpret_cast<float4*>(dx + m * lddx + 4 * q) = make_float4(v[0], v[1], v[2], v[3]);
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int q = q0 + 32 * u;
+        if (q >= nq) break;
+        float4 w[NB];
+#pragma unroll
+        for (int n = 0; n < NB; ++n) w[n] = *reinterpret_cast<const float4*>(&Wt[n * ldt + 4 * q]);
+#pragma unroll
+        for (int r = 0; r < RPW; ++r) {
+          const int64_t m = m_base + r;
+          if (m >= M) break;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int n = 0; n < NB; ++n) {
+            v[0] = fmaf(dzv[r][n], w[n].x, v[0]);
+            v[1] = fmaf(dzv[r][n], w[n].y, v[1]);
+            v[2] = fmaf(dzv[r][n], w[n].z, v[2]);
+            v[3] = fmaf(dzv[r][n], w[n].w, v[3]);
+          }
+          const float4 k4 = mk[u][r];
+          v[0] = __fmul_rn(__fadd_rn(v[0], 0.f), k4.x > 0.f ? 1.f : 0.f);
+          v[1] = __fmul_rn(__fadd_rn(v[1], 0.f), k4.y > 0.f ? 1.f : 0.f);
+          v[2] = __fmul_rn(__fadd_rn(v[2], 0.f), k4.z > 0.f ? 1.f : 0.f);
+          v[3] = __fmul_rn(__fadd_rn(v[3], 0.f), k4.w > 0.f ? 1.f : 0.f);
+          *reinterpret_cast<float4*>(dx + m * lddx + 4 * q) = make_float4(v[0], v[1], v[2], v[3]);
+        }
       }
     }
   }
