@@ -425,6 +425,32 @@ def hidden_gemm(tl, P, M, scheme, check: bool):
     return res
 
 
+def allreduce_alone(tl, P, comm, rdv, calls=10):
+    """The gradient arena's all-reduce timed alone on the communication stream
+    (CUDA events, max over ranks, after 3 untimed calls): bytes, ms and bus
+    bandwidth (2 (n-1)/n of the bytes cross each GPU's links each way).  It
+    sums into the gradients, so it runs after the timed steps."""
+    rt = tl.runtime
+    L = rt.lib()
+    names = P.arena_names
+    p0 = P.ptr(names[0])
+    count = (P.ptr(names[-1]) - p0) // 4 + int(np.prod(P.shapes[names[-1]]))
+    call = lambda: rt.check(L.tl_nccl_allreduce_sum(comm.handle, p0, count, comm.stream),  # noqa: E731
+                            "allreduce")
+    for _ in range(3):
+        call()
+    rt.check(L.tl_stream_sync(comm.stream), "sync")
+    rdv.barrier()
+    ms = time_events(tl, comm.stream, call, calls)
+    every = rdv.gather(ms)
+    ms = max(every) if every else 0.0
+    n = comm.world
+    nbytes = 4 * count
+    bus = nbytes * 2 * (n - 1) / n / (ms * 1e-3) / 1e9 if ms else 0.0
+    return {"bytes": nbytes, "ms": ms, "busbw_gbs": bus, "calls": calls,
+            "note": "NCCL ring/tree over NVLink, NVLS off; timed alone, not overlapped"}
+
+
 def time_training(tl, loop, stream, steps, clocks=None):
     def timed_step():
         loop.replay(1)
@@ -585,6 +611,8 @@ def run_ours(args, rank, world, local):
     rdv.barrier()
     all_e2e = rdv.gather(e2e_ms)
     loss = float(P.read("loss").reshape(-1)[0])
+    graph_nodes = loop.graph_nodes
+    ar = allreduce_alone(tl, P, comm, rdv) if world > 1 else None
 
     # dominant kernel: the hidden-layer GEMM (b x 4096 x 4096), timed alone
     roof = hidden_gemm(tl, P, b, args.gemm_scheme, check=(rank == 0 and not args.no_check))
@@ -599,7 +627,7 @@ def run_ours(args, rank, world, local):
 
     if rank == 0:
         cpu = None
-        if not args.no_cpu:
+        if not args.no_cpu and world == 1:
             t = cpu_mlp_step_times(1, 0)[0]
             cpu = {"value": 1.0 / t, "unit": "steps/s", "cores": os.cpu_count() or 1, "kind": "port",
                    "sample": f"one full-batch ({B_GLOBAL}-row) training step of the float32 NumPy "
@@ -627,9 +655,14 @@ def run_ours(args, rank, world, local):
                     "h2d_bytes_per_step": int(xs.nbytes + ts.nbytes) * world,
                     "d2h_bytes_per_step": 4 * world},
             "gpu_launches": int(launches_per_step * args.steps),
+            "graph": {"kernel_nodes": graph_nodes[0], "prioritised": graph_nodes[1],
+                      "allreduce_buckets": sum(1 for s in P._all_steps()
+                                               if type(s).__name__ == "AllReduceBucket")},
             "clocks": clk,
             "cpu_baseline": cpu,
         }
+        if ar is not None:
+            line["allreduce"] = ar
         line.update(extra)
         print(json.dumps(line), flush=True)
     comm.destroy()

@@ -85,6 +85,12 @@ int  tl_graph_begin(void* stream);
 int  tl_graph_end(void* stream, void** graph_exec);
 int  tl_graph_launch(void* graph_exec, void* stream);
 int  tl_graph_destroy(void* graph_exec);
+/* Graphs are instantiated with the nodes' own priorities, so that kernels
+ * captured from tl_stream_create_priority(urgent) streams (the gradient
+ * all-reduce) keep their priority when the graph replays.  Kernel nodes of
+ * the last graph captured on the calling thread, and how many of them carry
+ * a non-default priority. */
+int  tl_graph_last_stats(int* kernel_nodes, int* prioritised_nodes);
 
 /* Number of kernels this library has launched on the calling thread since
  * the last reset (graph replays are not counted). */

@@ -234,11 +234,35 @@ int tl_graph_begin(void* stream) {
   TL_CUDA_TRY(cudaStreamBeginCapture(tl::stream_or_default(stream), cudaStreamCaptureModeThreadLocal));
   return TL_OK;
 }
+// kernel nodes of the last captured graph, and how many of them carry a
+// priority other than the default (captured from a priority stream)
+static thread_local int t_graph_kernels = 0, t_graph_prioritised = 0;
+
 int tl_graph_end(void* stream, void** graph_exec) {
   cudaGraph_t g = nullptr;
   TL_CUDA_TRY(cudaStreamEndCapture(tl::stream_or_default(stream), &g));
+  t_graph_kernels = t_graph_prioritised = 0;
+  size_t n = 0;
+  if (cudaGraphGetNodes(g, nullptr, &n) == cudaSuccess && n > 0) {
+    std::vector<cudaGraphNode_t> nodes(n);
+    if (cudaGraphGetNodes(g, nodes.data(), &n) == cudaSuccess) {
+      for (size_t i = 0; i < n; ++i) {
+        cudaGraphNodeType ty;
+        if (cudaGraphNodeGetType(nodes[i], &ty) != cudaSuccess || ty != cudaGraphNodeTypeKernel) continue;
+        ++t_graph_kernels;
+        cudaLaunchAttributeValue v{};
+        if (cudaGraphKernelNodeGetAttribute(nodes[i], cudaLaunchAttributePriority, &v) == cudaSuccess &&
+            v.priority != 0)
+          ++t_graph_prioritised;
+      }
+    }
+  }
+  cudaGetLastError();
   cudaGraphExec_t ex = nullptr;
-  cudaError_t e = cudaGraphInstantiate(&ex, g, 0ULL);
+  // node priorities as captured: the gradient all-reduce's kernels keep the
+  // communication stream's priority inside the graph (by default a graph runs
+  // every node at the priority of the stream it is launched into)
+  cudaError_t e = cudaGraphInstantiate(&ex, g, (unsigned long long)cudaGraphInstantiateFlagUseNodePriority);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) return (int)e;
   *graph_exec = (void*)ex;
@@ -250,6 +274,12 @@ int tl_graph_launch(void* graph_exec, void* stream) {
 }
 int tl_graph_destroy(void* graph_exec) {
   TL_CUDA_TRY(cudaGraphExecDestroy((cudaGraphExec_t)graph_exec));
+  return TL_OK;
+}
+
+int tl_graph_last_stats(int* kernel_nodes, int* prioritised_nodes) {
+  if (kernel_nodes) *kernel_nodes = t_graph_kernels;
+  if (prioritised_nodes) *prioritised_nodes = t_graph_prioritised;
   return TL_OK;
 }
 

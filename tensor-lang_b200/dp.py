@@ -10,11 +10,11 @@ priority.  By default one all-reduce covers the whole gradient arena at the
 end of backward; with ``bucket_bytes`` the gradients are grouped into buckets
 in the order backward finalises them (weight gradients before each layer's
 dX) and each bucket's all-reduce starts as soon as its last gradient is
-written.  Measured on 8 B200s with the 3-layer MLP (per-GPU batch 8192, 3.4
-ms of compute a step): one 84 MB all-reduce alone takes 0.30 ms, 64 + 16 MB
-buckets 0.39 ms, and bucketed overlap -- at default or highest stream
-priority -- gave the same step time (4.1-4.3 ms) as the single all-reduce, so
-the single one is the default.  The cross_entropy and mse_loss
+written.  Measured with the 3-layer MLP at 8192 rows per rank: the 84 MB
+all-reduce alone takes 0.19-0.20 ms on 2 B200s (ring, 32 channels), the
+step 2.72-2.78 ms with one all-reduce against 2.46 ms without, and 2.69-2.75
+ms with buckets: NCCL's blocks hold SMs the concurrent CTA-pair GEMMs need,
+so the single all-reduce is the default.  The cross_entropy and mse_loss
 VJPs divide by the *global* batch (autograd.py:686,700), so the summed
 gradients equal the single-GPU ones and the replicated SGD update keeps the
 replicas identical.
@@ -251,8 +251,10 @@ def plan_buckets(bw: List[Step], grads: Sequence[str], shapes: Dict[str, Shape],
     gradients are taken in the order they become final, and a bucket closes
     (its all-reduce is inserted right after that step) once it holds
     ``bucket_bytes`` (None: one bucket for everything, issued at the end);
-    what is left joins the last bucket, issued at the end.  Returns the new
-    step list and the arena order (buckets contiguous)."""
+    what is left is a bucket of its own, issued at the end (joining it to the
+    last full bucket would move that bucket's all-reduce to the end too, where
+    nothing overlaps it).  Returns the new step list and the arena order
+    (buckets contiguous)."""
     last = {}
     for i, st in enumerate(bw):
         for n in set(st.reads) | set(st.writes):
@@ -267,10 +269,7 @@ def plan_buckets(bw: List[Step], grads: Sequence[str], shapes: Dict[str, Shape],
             buckets.append(cur)
             cur, size = [], 0
     if cur:
-        if buckets:
-            buckets[-1] = buckets[-1] + cur  # the tail goes out with the last bucket
-        else:
-            buckets.append(cur)
+        buckets.append(cur)
     after = {}
     for bi, names in enumerate(buckets):
         pos = max(last.get(n, -1) for n in names)

@@ -136,6 +136,7 @@ class _Loop(Step):
         self.reads = sorted({r for s in self.body() for r in s.reads})
         self.writes = sorted({w for s in self.body() for w in s.writes})
         self.graph = None
+        self.graph_nodes = (0, 0)
 
     def body(self) -> List[Step]:
         return self.pre + self.bw + self.post + self.rebind
@@ -179,6 +180,9 @@ class _Loop(Step):
             ge = ctypes.c_void_p()
             rt.check(rt.lib().tl_graph_end(self._stream, ctypes.byref(ge)), "graph_end")
         self.graph = ge.value
+        k, pr = ctypes.c_int(), ctypes.c_int()
+        rt.check(rt.lib().tl_graph_last_stats(ctypes.byref(k), ctypes.byref(pr)), "graph_stats")
+        self.graph_nodes = (k.value, pr.value)  # kernel nodes, of them prioritised
 
     def replay(self, n: int = 1):
         L = rt.lib()

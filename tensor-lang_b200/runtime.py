@@ -72,6 +72,7 @@ _SIGS = [
     ("tl_stream_wait_event", c_int, [c_void_p, c_void_p]),
     ("tl_graph_begin", c_int, [c_void_p]),
     ("tl_graph_end", c_int, [c_void_p, ctypes.POINTER(c_void_p)]),
+    ("tl_graph_last_stats", c_int, [ctypes.POINTER(c_int), ctypes.POINTER(c_int)]),
     ("tl_graph_launch", c_int, [c_void_p, c_void_p]),
     ("tl_graph_destroy", c_int, [c_void_p]),
     ("tl_launch_counter", c_int, [ctypes.POINTER(c_uint64), c_int]),

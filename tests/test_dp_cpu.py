@@ -139,7 +139,7 @@ def test_sharded_gradient_sum_equals_full_batch():
 def test_bucket_plan_overlaps_backward():
     """Gradient all-reduces are bucketed in the order backward finalises the
     gradients; a bucket is issued right after its last gradient is written,
-    the tail rides with the last bucket, and a join closes the list."""
+    the tail is a bucket of its own at the end, and a join closes the list."""
     from conftest import load_backend
     tl = load_backend()
     from tensor_lang_b200 import dp
@@ -176,6 +176,15 @@ def test_bucket_plan_overlaps_backward():
                 continue
             assert not (set(b.names) & (set(s.reads) | set(s.writes))), (b.label, s.label)
     assert sum(4 * numel(P.shapes[n]) for n in first.names) >= dp.BUCKET_BYTES
+    # the last bucket is the tail, issued right before the join
+    assert steps.index(buckets[-1]) == len(steps) - 2
+    # a 64 MB bucket: W2 closes it, the rest (b2, W1, b1) is the tail
+    steps64, _ = dp.plan_buckets(list(bw), grads, P.shapes, _Comm(), 64 << 20)
+    b64 = [s for s in steps64 if isinstance(s, dp.AllReduceBucket)]
+    assert len(b64) == 2 and "W2_grad" in b64[0].names
+    assert sorted(b64[1].names) == ["W1_grad", "b1_grad", "b2_grad"]
+    assert steps64.index(b64[1]) == len(steps64) - 2
+    assert steps64.index(b64[0]) < len(steps64) - 3
 
 
 def test_only_parameter_gradients_are_all_reduced():
