@@ -643,6 +643,9 @@ def run_ours(args, rank, world, local):
             "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL,
                        "per_gpu_batch": b, "dims": [D_IN, D_H, D_H, N_CLS],
                        "parallelism": f"dp{world}", "gemm": f"{scheme[1]}, CTA-pair 256x256 tiles",
+                       "gradient_allreduce": (f"buckets of {args.bucket_mb:g} MiB as backward "
+                                              "finalises them" if args.bucket_mb
+                                              else "one, after backward"),
                        "l2": "inputs larger than L2 (no flush)"},
             "model_tflops": FLOP_PER_STEP / (ms_max * 1e-3) / 1e12,
             "loss_rank0": loss,
@@ -767,7 +770,7 @@ def main():
     ap.add_argument("--no-check", action="store_true", help="skip the GEMM error check")
     ap.add_argument("--no-head-fusion", action="store_true",
                     help="profiling aid: run the classifier head unfused")
-    ap.add_argument("--bucket-mb", type=float, default=0,
+    ap.add_argument("--bucket-mb", type=float, default=64,
                     help="data parallel: all-reduce gradients in buckets of this many MiB as "
                          "backward finalises them (0: one all-reduce after backward)")
     ap.add_argument("--gemm-m", type=int, default=8192, help="rows of the --micro gemm product")

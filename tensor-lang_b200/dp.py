@@ -6,15 +6,15 @@ tensors is split contiguously (rank r holds rows [r*B/P, (r+1)*B/P)), every
 rank holds full parameter replicas, and the gradients of the replicated
 tensors are summed across ranks by NCCL all-reduces over NVLink (libtlb200
 ``tl_nccl_allreduce_sum``) on a communication stream of the highest
-priority.  By default one all-reduce covers the whole gradient arena at the
-end of backward; with ``bucket_bytes`` the gradients are grouped into buckets
-in the order backward finalises them (weight gradients before each layer's
-dX) and each bucket's all-reduce starts as soon as its last gradient is
-written.  Measured with the 3-layer MLP at 8192 rows per rank: the 84 MB
-all-reduce alone takes 0.19-0.20 ms on 2 B200s (ring, 32 channels), the
-step 2.72-2.78 ms with one all-reduce against 2.46 ms without, and 2.69-2.75
-ms with buckets: NCCL's blocks hold SMs the concurrent CTA-pair GEMMs need,
-so the single all-reduce is the default.  The cross_entropy and mse_loss
+priority.  The gradients are grouped into buckets (64 MiB by default) in
+the order backward finalises them (weight gradients before each layer's dX)
+and each bucket's all-reduce starts as soon as its last gradient is written;
+``bucket_bytes=None`` sends the whole arena in one all-reduce after
+backward.  Measured with the 3-layer MLP at 8192 rows per rank on 2 B200s:
+the 84 MB all-reduce alone takes 0.19-0.20 ms (ring, 32 channels); the step
+takes 2.46 ms without it, 2.72-2.78 ms with one all-reduce and 2.67-2.70 ms
+with 64 MiB buckets (the first, 64 MB, overlaps the dX GEMM; the 16 MB tail
+goes out at the end).  The cross_entropy and mse_loss
 VJPs divide by the *global* batch (autograd.py:686,700), so the summed
 gradients equal the single-GPU ones and the replicated SGD update keeps the
 replicas identical.
@@ -239,7 +239,7 @@ class AllReduceJoin(Step):
         return run
 
 
-BUCKET_BYTES = 16 << 20  # a bucket closes once it holds this much (bucketed mode)
+BUCKET_BYTES = 64 << 20  # a bucket closes once it holds this much (bucketed mode)
 
 
 def plan_buckets(bw: List[Step], grads: Sequence[str], shapes: Dict[str, Shape],
@@ -371,7 +371,7 @@ class DataParallelProgram:
     def __init__(self, ast: list, env: Optional[dict], comm: Communicator, *, device: int,
                  feeds: Dict[str, np.ndarray], fetch: Optional[Sequence[str]] = None,
                  sharded: Sequence[str] = ("x", "t"), use_graphs: bool = True,
-                 bucket_bytes: Optional[int] = None, fuse_head: bool = True):
+                 bucket_bytes: Optional[int] = BUCKET_BYTES, fuse_head: bool = True):
         self.comm = comm
         gshapes = complete_env(ast, env or {})
         self.derived = batch_derived(ast, sharded)

@@ -209,4 +209,6 @@ def test_only_parameter_gradients_are_all_reduced():
     assert sum(numel(P.shapes[n]) for n in P.arena_names) == 21_020_682
     P._fuse_all()
     ar = [s for s in P._all_steps() if isinstance(s, dp.AllReduceBucket)]
-    assert len(ar) == 1 and sorted(ar[0].names) == sorted(D.replicated_grads)
+    # default 64 MiB buckets: W3, b3 and W2 (after dW2), then b2, W1 and b1
+    assert len(ar) == 2 and sorted(n for b in ar for n in b.names) == sorted(D.replicated_grads)
+    assert [n for b in ar for n in b.names] == P.arena_names
