@@ -71,11 +71,6 @@ def set_tile_schedule(tl, name):
                      "tile schedule")
 
 
-def set_l2_policy(tl, name):
-    tl.runtime.check(tl.runtime.lib().tl_gemm_set_l2_policy(1 if name == "keep-b" else 0, None),
-                     "l2 policy")
-
-
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -577,7 +572,6 @@ def run_ours(args, rank, world, local):
     rt = tl.runtime
     set_gemm_scheme(tl, args.gemm_scheme)
     set_tile_schedule(tl, args.tile_schedule)
-    set_l2_policy(tl, args.l2_policy)
     from tensor_lang_b200 import dp
 
     dev = local
@@ -649,8 +643,7 @@ def run_ours(args, rank, world, local):
             "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL,
                        "per_gpu_batch": b, "dims": [D_IN, D_H, D_H, N_CLS],
                        "parallelism": f"dp{world}", "gemm": f"{scheme[1]}, CTA-pair 256x256 tiles",
-                       "gradient_allreduce": ("none (one GPU)" if world == 1 else
-                                              f"buckets of {args.bucket_mb:g} MiB as backward "
+                       "gradient_allreduce": (f"buckets of {args.bucket_mb:g} MiB as backward "
                                               "finalises them" if args.bucket_mb
                                               else "one, after backward"),
                        "l2": "inputs larger than L2 (no flush)"},
@@ -699,7 +692,6 @@ def run_micro(args):
     st = dev.stream
     set_gemm_scheme(tl, args.gemm_scheme)
     set_tile_schedule(tl, args.tile_schedule)
-    set_l2_policy(tl, args.l2_policy)
     hbm, bf16, _, src = peaks()
     reps = args.steps
     if args.micro == "reductions":
@@ -788,9 +780,6 @@ def main():
                          "work of eight)")
     ap.add_argument("--gemm-scheme", choices=sorted(GEMM_SCHEMES), default="bf16x3",
                     help="tensor-core operand scheme of the fp32 GEMMs")
-    ap.add_argument("--l2-policy", choices=("keep-b", "none"), default="keep-b",
-                    help="CTA-pair GEMMs: keep a small B operand in L2 (evict-last) or "
-                         "give no cache hints")
     ap.add_argument("--tile-schedule", choices=sorted(TILE_SCHEDULES), default="auto",
                     help="CTA-pair GEMM tile schedule: static groups, dynamic (running "
                          "clusters take pending clusters' tiles), or auto (the library's choice "

@@ -330,13 +330,6 @@ int  tl_gemm_set_cta_pair(int enable, int* previous);
  * every schedule.  *previous (if non-null) receives the setting that was in
  * force. */
 int  tl_gemm_set_tile_schedule(int dynamic, int* previous);
-/* L2 cache policy of CTA-pair launches (no reference counterpart).  keep_small_b = 1 (default): when B's bf16 pair is at most
- * 72 MiB and A has at least as many rows as B has columns, B's pair tiles
- * are loaded with an evict-last policy, so the B pair stays in L2 across
- * waves instead of being read from DRAM once per wave; 0: no hints.
- * Results are bit-identical either way.  *previous (if non-null) receives
- * the setting that was in force. */
-int  tl_gemm_set_l2_policy(int keep_small_b, int* previous);
 /* ---- classifier head of a training step, fused ---------------------------
  * linear (kernel_generator.py:1584-1661) with N <= 16 outputs, row softmax
  * (:564-640) and cross_entropy (:1816-1885), and their backward:

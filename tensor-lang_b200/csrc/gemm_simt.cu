@@ -29,7 +29,6 @@ void gemm_set_split_mode(int mode);
 int gemm_set_scheme(int scheme);
 int gemm_set_cta_pair(int enable);
 int gemm_set_tile_dynamic(int enable);
-int gemm_set_l2_keep(int mode);
 int gemm_small(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
                int accumulate, int epilogue, const float* mask, int64_t ldm, cudaStream_t st);
@@ -246,13 +245,6 @@ int tl_gemm_set_cta_pair(int enable, int* previous) {
 int tl_gemm_set_tile_schedule(int dynamic, int* previous) {
   if (dynamic < 0 || dynamic > 2) return TL_ERR_INVALID_ARG;
   const int prev = tl::gemm_set_tile_dynamic(dynamic);
-  if (previous) *previous = prev;
-  return TL_OK;
-}
-
-int tl_gemm_set_l2_policy(int keep_small_b, int* previous) {
-  if (keep_small_b < 0 || keep_small_b > 1) return TL_ERR_INVALID_ARG;
-  const int prev = tl::gemm_set_l2_keep(keep_small_b);
   if (previous) *previous = prev;
   return TL_OK;
 }

@@ -276,8 +276,6 @@ struct Params {
   float* partial;     // [splits][M][N] raw sums when splits > 1
   int tpc = 1;        // CTA-pair kernel: tiles each cluster computes in turn
   int clc = 0;        // CTA-pair kernel: take pending clusters' tiles (cluster launch control)
-  int keep_b = 0;     // CTA-pair kernel: B's pair tiles loaded with an L2 evict-last policy
-                      // (a small B that every wave of tiles reads again)
 };
 
 // Split-K partial of one thread's BN/2 columns of row `row` (no epilogue).
@@ -646,21 +644,6 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
-// The same load with an L2 cache policy (createpolicy): evict-last keeps a
-// tile that later waves read again.
-__device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap* map,
-                                                      uint32_t bar, int c0, int c1, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
-      "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1), "l"(pol)
-      : "memory");
-}
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-  uint64_t pol;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol));
-  return pol;
-}
 __device__ __forceinline__ void mma2_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -812,7 +795,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint32_t full0 = mapa_shared(smem_u32(&full[0]), 0);  // the leader's full[0]
-      const uint64_t pol_b = l2_policy_evict_last();
       bool ok = true;
       int it = 0;
       for (int grp = cid, r = 0; ok; ++r) {
@@ -860,22 +842,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
               if (!PAIR) tma_load_2d_pair(sBx + c * 4096, &tmBx, fb, nb + 32 * c, k0);
             }
           }
-          if (PAIR && p.keep_b) {
-            if (TA == 0) {
-              tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
-            } else {
-#pragma unroll
-              for (int c = 0; c < BM / 64; ++c)
-                tma_load_2d_pair(sAx + c * PAIR_MN_CHUNK, &tmAx, fb, m0 + 64 * c, 2 * k0);
-            }
-            if (TB == 1) {
-              tma_load_2d_pair_hint(sBx, &tmBx, fb, 2 * k0, nb, pol_b);
-            } else {
-#pragma unroll
-              for (int c = 0; c < HB / 64; ++c)
-                tma_load_2d_pair_hint(sBx + c * PAIR_MN_CHUNK, &tmBx, fb, nb + 64 * c, 2 * k0, pol_b);
-            }
-          } else if (PAIR) {
+          if (PAIR) {
             if (TA == 0) {
               tma_load_2d_pair(sAx, &tmAx, fb, 2 * k0, m0);
             } else {
@@ -1380,19 +1347,6 @@ int g_tiles_per_cluster = 4;  // upper bound on the tiles one CTA pair computes 
 // control), so an SM pair computes tiles back to back until none are left;
 // 2 (default) dynamic where it measured faster (use_dynamic)
 int g_tile_dynamic = 2;
-// L2 policy of CTA-pair launches: 1 (default) loads a small B's pair
-// (keep_b_in_l2) with evict-last, 0 no hints
-int g_l2_keep = 1;
-
-// A launch's concurrent tiles span all column blocks of a few row blocks
-// (dynamic schedule) or of a few more (static, four tiles per cluster), so
-// every wave reads the whole B pair again; when B's pair fits
-// well inside the 126 MB L2 and A is at least as large, keeping B resident
-// turns those re-reads into L2 hits (A's k-slices are shared by the
-// concurrent tiles of a row block within microseconds and need no hint).
-bool keep_b_in_l2(int64_t M, int64_t N, int64_t K) {
-  return g_l2_keep && N * K * 4 <= (72LL << 20) && M >= N;
-}
 
 // Tiles per cluster for a CTA-pair launch of `tiles` tiles: each cluster
 // launch pays a prologue (barrier set-up, TMEM allocation, pipeline fill) and
@@ -1456,7 +1410,6 @@ int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CU
     q.splits = splits;
     q.clc = use_dynamic(clusters * splits, p.K) ? 1 : 0;
     q.tpc = q.clc ? 1 : tiles_per_cluster(clusters * splits);
-    q.keep_b = keep_b_in_l2(M, N, p.K) ? 1 : 0;
     const int64_t launched = (clusters * splits + q.tpc - 1) / q.tpc;  // clusters launched
     if (splits > 1) {
       float* part = nullptr;
@@ -1681,12 +1634,6 @@ void gemm_set_split_mode(int mode) { g_split_mode = mode; }
 int gemm_set_cta_pair(int enable) {
   const int prev = g_cta_pair;
   g_cta_pair = enable ? 1 : 0;
-  return prev;
-}
-
-int gemm_set_l2_keep(int mode) {
-  const int prev = g_l2_keep;
-  g_l2_keep = mode ? 1 : 0;
   return prev;
 }
 

@@ -298,45 +298,3 @@ def test_gemm_dynamic_schedule_accumulate_and_plan():
     assert err == 0 and path == 0
     assert_close(out, ref, 1e-5, "dynamic schedule, accumulate")
     assert plan[2] == 1 and plan[3] == 4096, "one tile per cluster launch"
-
-
-class _L2Policy:
-    """Select the CTA-pair L2 policy for the duration of a with-block."""
-
-    def __init__(self, keep_small_b):
-        self.keep = keep_small_b
-
-    def __enter__(self):
-        tl = load_backend()
-        self.L = tl.runtime.lib()
-        self.prev = ctypes.c_int(-1)
-        tl.runtime.check(self.L.tl_gemm_set_l2_policy(self.keep, ctypes.byref(self.prev)))
-        return self
-
-    def __exit__(self, *exc):
-        self.L.tl_gemm_set_l2_policy(self.prev.value, None)
-        return False
-
-
-@pytest.mark.parametrize("dynamic", [0, 1])
-@pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0)])
-@pytest.mark.parametrize("M,N,K", [(4096, 4096, 2048), (18900, 4056, 520)])
-def test_gemm_l2_policy_is_bit_identical(dynamic, ta, tb, M, N, K):
-    """Loading B's pair with an L2 evict-last policy (the default where B's
-    pair is at most 72 MiB and A has at least N rows) changes only where the
-    lines live, not the product: bit-identical to the unhinted launch, under
-    both tile schedules, and within rel 1e-5 of float64."""
-    with _Schedule(dynamic):
-        with _L2Policy(0):
-            plain, ref, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
-        assert err == 0 and path == 0
-        with _L2Policy(1):
-            kept, _, path, err = _run(ta, tb, M, N, K, bias=True, relu=True)
-        assert err == 0 and path == 0
-    np.testing.assert_array_equal(kept, plain)
-    assert_close(kept, ref, 1e-5, f"L2 policy, schedule {dynamic} {ta}{tb} {M}x{N}x{K}")
-
-
-def test_gemm_l2_policy_rejects_unknown():
-    L = load_backend().runtime.lib()
-    assert L.tl_gemm_set_l2_policy(2, None) != 0
