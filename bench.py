@@ -643,7 +643,8 @@ def run_ours(args, rank, world, local):
             "config": {"workload": "mlp3_dp_train", "global_batch": B_GLOBAL,
                        "per_gpu_batch": b, "dims": [D_IN, D_H, D_H, N_CLS],
                        "parallelism": f"dp{world}", "gemm": f"{scheme[1]}, CTA-pair 256x256 tiles",
-                       "gradient_allreduce": (f"buckets of {args.bucket_mb:g} MiB as backward "
+                       "gradient_allreduce": ("none (one GPU)" if world == 1 else
+                                              f"buckets of {args.bucket_mb:g} MiB as backward "
                                               "finalises them" if args.bucket_mb
                                               else "one, after backward"),
                        "l2": "inputs larger than L2 (no flush)"},
