@@ -350,7 +350,8 @@ def fused_op_bench(tl, dev, reps=20):
     return res
 
 
-def build_training(tl, comm, dev, rank, world, epochs, bucket_mb=None, fuse_head=True):
+def build_training(tl, comm, dev, rank, world, epochs, bucket_mb=None, fuse_head=True,
+                   fuse_colsum=True):
     """The benchmark program on this rank's shard, prepared, with its first
     iteration run eagerly; returns (program, loop, feeds, kernel launches per
     iteration)."""
@@ -362,7 +363,7 @@ def build_training(tl, comm, dev, rank, world, epochs, bucket_mb=None, fuse_head
     feeds = pr.mlp3_inputs(B=B_GLOBAL, I=D_IN, H=D_H, C=N_CLS, seed=0, rows=(rank * b, (rank + 1) * b))
     D = dp.DataParallelProgram(ast, None, comm, device=dev, feeds=feeds, fetch=["loss", "W3"],
                                bucket_bytes=None if not bucket_mb else int(bucket_mb * (1 << 20)),
-                               fuse_head=fuse_head)
+                               fuse_head=fuse_head, fuse_colsum=fuse_colsum)
     P = D.program
     P.prepare()
     loop = P.loops[0]
@@ -585,7 +586,8 @@ def run_ours(args, rank, world, local):
     P, loop, feeds, launches_per_step = build_training(tl, comm, dev, rank, world,
                                                        epochs=1 + args.warmup + args.steps,
                                                        bucket_mb=args.bucket_mb,
-                                                       fuse_head=not args.no_head_fusion)
+                                                       fuse_head=not args.no_head_fusion,
+                                                       fuse_colsum=not args.no_colsum_fusion)
     stream = P.stream
     for _ in range(args.warmup):
         loop.replay(1)
@@ -769,6 +771,9 @@ def main():
     ap.add_argument("--no-cpu-configs", action="store_true",
                     help="--impl reference: skip the other workloads")
     ap.add_argument("--no-check", action="store_true", help="skip the GEMM error check")
+    ap.add_argument("--no-colsum-fusion", action="store_true",
+                    help="keep each bias gradient's column sum as its own pass over dY instead "
+                         "of folding it into the pair step of dY")
     ap.add_argument("--no-head-fusion", action="store_true",
                     help="profiling aid: run the classifier head unfused")
     ap.add_argument("--bucket-mb", type=float, default=64,

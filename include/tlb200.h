@@ -268,6 +268,20 @@ int64_t tl_gemm_pair_bytes(int64_t rows, int64_t cols, int layout);
 int  tl_gemm_pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols,
                           void* kmajor, int kmajor_lo_first, void* mnmajor,
                           int mnmajor_lo_first, void* stream);
+/* tl_gemm_pair_prepare that also writes colsum[c] = sum over rows of X[r][c]
+ * (summed in double, rounded once) from the same read of X: the bias
+ * gradient db of a linear layer (autograd.py:619-646, replacing the separate
+ * tl_reduce_cols sum over the same dY that the reference's backward runs).
+ * scratch: at least tl_gemm_pair_colsum_scratch_bytes(rows, cols) bytes,
+ * 8-byte aligned (per-block partial sums); cols up to 8192.  The result may
+ * differ from tl_reduce_cols(TL_RED_SUM) in the last bit of a float where
+ * the two double sums round differently.  No reference counterpart as a
+ * single call. */
+size_t tl_gemm_pair_colsum_scratch_bytes(int64_t rows, int64_t cols);
+int  tl_gemm_pair_prepare_colsum(const float* X, int64_t ld, int64_t rows, int64_t cols,
+                                 void* kmajor, int kmajor_lo_first, void* mnmajor,
+                                 int mnmajor_lo_first, float* colsum, void* scratch,
+                                 size_t scratch_bytes, void* stream);
 int  tl_gemm_pairs(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K,
                    const float* A, int64_t lda, const void* a_pair,
                    const float* B, int64_t ldb, const void* b_pair,

@@ -23,6 +23,10 @@ int gemm_tc_plan(int64_t M, int64_t N, int64_t K, int* out);
 int64_t pair_bytes(int64_t rows, int64_t cols, int layout);
 int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
                  int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st);
+size_t pair_colsum_scratch_bytes(int64_t rows, int64_t cols);
+int pair_prepare_colsum(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                        int k_lo_first, void* mnmajor, int m_lo_first, float* colsum,
+                        void* scratch, size_t scratch_bytes, cudaStream_t st);
 bool gemm_tc_ok(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                 const float* B, int64_t ldb, const float* C, int64_t ldc);
 void gemm_set_split_mode(int mode);
@@ -208,6 +212,24 @@ int tl_gemm_pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols,
   if ((((uintptr_t)kmajor) & 15) || (((uintptr_t)mnmajor) & 15)) return TL_ERR_INVALID_ARG;
   return tl::pair_prepare(X, ld, rows, cols, kmajor, kmajor_lo_first, mnmajor, mnmajor_lo_first,
                           tl::stream_or_default(stream));
+}
+
+size_t tl_gemm_pair_colsum_scratch_bytes(int64_t rows, int64_t cols) {
+  if (rows <= 0 || cols <= 0) return 0;
+  return tl::pair_colsum_scratch_bytes(rows, cols);
+}
+
+int tl_gemm_pair_prepare_colsum(const float* X, int64_t ld, int64_t rows, int64_t cols,
+                                void* kmajor, int kmajor_lo_first, void* mnmajor,
+                                int mnmajor_lo_first, float* colsum, void* scratch,
+                                size_t scratch_bytes, void* stream) {
+  if (!X || !colsum || !scratch || rows <= 0 || cols <= 0 || ld < cols || (!kmajor && !mnmajor))
+    return TL_ERR_INVALID_ARG;
+  if ((((uintptr_t)kmajor) & 15) || (((uintptr_t)mnmajor) & 15) || (((uintptr_t)scratch) & 7))
+    return TL_ERR_INVALID_ARG;
+  return tl::pair_prepare_colsum(X, ld, rows, cols, kmajor, kmajor_lo_first, mnmajor,
+                                 mnmajor_lo_first, colsum, scratch, scratch_bytes,
+                                 tl::stream_or_default(stream));
 }
 
 int tl_gemm(int trans_a, int trans_b, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,

@@ -52,6 +52,7 @@
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <vector>
 
@@ -1248,6 +1249,104 @@ __global__ void __launch_bounds__(256) pair_both_kernel(const float* __restrict_
   }
 }
 
+// pair_both_kernel that also sums the columns of X (the bias gradient
+// db = sum over rows of dY, autograd.py:619-646) from the same read: each
+// block accumulates, in double, the columns of its threads over the rows it
+// converts (rows blockIdx.x + k * gridDim.x) and writes them as one row of
+// `part` ([gridDim.x][C] doubles); colsum_finish_kernel adds those rows.
+// J: column steps of 2048 per thread (c_end <= 2048 * J).
+template <int J>
+__global__ void __launch_bounds__(256) pair_colsum_kernel(const float* __restrict__ X, int64_t ld,
+                                                          int64_t R, int64_t C,
+                                                          __nv_bfloat16* __restrict__ pk,
+                                                          int k_lo_first,
+                                                          __nv_bfloat16* __restrict__ pm,
+                                                          int m_lo_first, int lo_mode,
+                                                          double* __restrict__ part) {
+  const bool vec = (ld % 4 == 0) && (((uintptr_t)X & 15) == 0);
+  const int64_t kpc = (C + 31) / 32 * 32;
+  const int64_t rp = (C + 7) / 8 * 8;
+  const int64_t r_end = pm ? (R + 31) / 32 * 32 : R;
+  const int64_t c_end = pk ? kpc : rp;
+  double acc[J][8];
+#pragma unroll
+  for (int j = 0; j < J; ++j)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[j][i] = 0.0;
+  for (int64_t r = blockIdx.x; r < r_end; r += gridDim.x) {
+    const float* src = X + r * ld;
+    __nv_bfloat16* kv = pk ? pk + r * 2 * kpc : nullptr;
+    __nv_bfloat16* mv = pm ? pm + (64 * (r >> 5) + (r & 31)) * rp : nullptr;
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int64_t c = 8 * (int64_t)threadIdx.x + 2048 * (int64_t)j;
+      if (c >= c_end) continue;
+      float x[8];
+      if (r < R && vec && c + 7 < C) {
+        const float4 a = ld_stream4(src + c), b = ld_stream4(src + c + 4);
+        x[0] = a.x; x[1] = a.y; x[2] = a.z; x[3] = a.w;
+        x[4] = b.x; x[5] = b.y; x[6] = b.z; x[7] = b.w;
+      } else {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) x[i] = (r < R && c + i < C) ? src[c + i] : 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[j][i] += (double)x[i];  // padding adds zeros
+      const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
+                                  pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
+      const uint4 lv = make_uint4(pack_bf16(lo_of(x[0], lo_mode), lo_of(x[1], lo_mode)),
+                                  pack_bf16(lo_of(x[2], lo_mode), lo_of(x[3], lo_mode)),
+                                  pack_bf16(lo_of(x[4], lo_mode), lo_of(x[5], lo_mode)),
+                                  pack_bf16(lo_of(x[6], lo_mode), lo_of(x[7], lo_mode)));
+      if (kv && r < R) {
+        __nv_bfloat16* o = kv + 64 * (c >> 5) + (c & 31);
+        *reinterpret_cast<uint4*>(o) = k_lo_first ? lv : hv;
+        *reinterpret_cast<uint4*>(o + 32) = k_lo_first ? hv : lv;
+      }
+      if (mv && c < rp) {
+        *reinterpret_cast<uint4*>(mv + c) = m_lo_first ? lv : hv;
+        *reinterpret_cast<uint4*>(mv + 32 * rp + c) = m_lo_first ? hv : lv;
+      }
+    }
+  }
+  double* prow = part + (int64_t)blockIdx.x * C;
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int64_t c = 8 * (int64_t)threadIdx.x + 2048 * (int64_t)j;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (c + i < C) prow[c + i] = acc[j][i];
+  }
+}
+
+// out[c] = sum of part[b][c] over b < G, in double, in a fixed order (warp w
+// adds rows w, w + 32, ... in turn; then warps 0..31 in turn): 32 columns per
+// block, one per lane.
+__global__ void __launch_bounds__(1024) colsum_finish_kernel(const double* __restrict__ part,
+                                                             int64_t G, int64_t C,
+                                                             float* __restrict__ out) {
+  __shared__ double sh[32][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int64_t c = (int64_t)blockIdx.x * 32 + lane;
+  double s = 0.0;
+  if (c < C) {
+    int64_t b = w;
+    for (; b + 96 < G; b += 128) {  // four rows in flight, added in row order
+      const double v0 = part[b * C + c], v1 = part[(b + 32) * C + c];
+      const double v2 = part[(b + 64) * C + c], v3 = part[(b + 96) * C + c];
+      s += v0; s += v1; s += v2; s += v3;
+    }
+    for (; b < G; b += 32) s += part[b * C + c];
+  }
+  sh[w][lane] = s;
+  __syncthreads();
+  if (w == 0 && c < C) {
+    double t = sh[0][lane];
+    for (int k = 1; k < 32; ++k) t += sh[k][lane];
+    out[c] = (float)t;
+  }
+}
+
 // ------------------------------------------------------------- host side ---
 typedef CUresult (*PFN_encodeTiled)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                     const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -1603,6 +1702,46 @@ int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* k
       X, ld, rows, cols, reinterpret_cast<__nv_bfloat16*>(kmajor), k_lo_first,
       reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first, g_scheme == kSchemeBF16X3 ? 1 : 0);
   return after_launch();
+}
+
+// Blocks of the pair pre-pass for rows x cols (and so rows of the column-sum
+// partials it writes).
+int64_t pair_grid(int64_t rows, bool mnmajor) {
+  const int64_t r_end = mnmajor ? (rows + 31) / 32 * 32 : rows;
+  const int64_t cap = 8LL * sm_count();
+  return r_end < cap ? r_end : cap;
+}
+
+size_t pair_colsum_scratch_bytes(int64_t rows, int64_t cols) {
+  return (size_t)pair_grid(rows, true) * (size_t)cols * sizeof(double);
+}
+
+int pair_prepare_colsum(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                        int k_lo_first, void* mnmajor, int m_lo_first, float* colsum,
+                        void* scratch, size_t scratch_bytes, cudaStream_t st) {
+  const int64_t g = pair_grid(rows, mnmajor != nullptr);
+  const int64_t c_end = kmajor ? (cols + 31) / 32 * 32 : (cols + 7) / 8 * 8;
+  if ((size_t)g * (size_t)cols * sizeof(double) > scratch_bytes) return TL_ERR_INVALID_ARG;
+  if (c_end > 4 * 2048) return TL_ERR_UNSUPPORTED;
+  double* part = static_cast<double*>(scratch);
+  auto* pk = reinterpret_cast<__nv_bfloat16*>(kmajor);
+  auto* pm = reinterpret_cast<__nv_bfloat16*>(mnmajor);
+  const int lo = g_scheme == kSchemeBF16X3 ? 1 : 0;
+  // one wave of resident blocks (the double sums take registers: fewer
+  // blocks fit an SM than pair_prepare's eight), each converting every
+  // g-th row
+  auto launch = [&](auto kern) -> int {
+    int per_sm = 0;
+    TL_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0));
+    const int64_t gg = std::min<int64_t>(g, (int64_t)std::max(per_sm, 1) * sm_count());
+    kern<<<(unsigned)gg, 256, 0, st>>>(X, ld, rows, cols, pk, k_lo_first, pm, m_lo_first, lo, part);
+    TL_TRY(after_launch());
+    colsum_finish_kernel<<<(unsigned)((cols + 31) / 32), 1024, 0, st>>>(part, gg, cols, colsum);
+    return after_launch();
+  };
+  if (c_end <= 2048) return launch(pair_colsum_kernel<1>);
+  if (c_end <= 4096) return launch(pair_colsum_kernel<2>);
+  return launch(pair_colsum_kernel<4>);
 }
 
 // The launch run_tiles makes for an M x N x K product on the tensor cores

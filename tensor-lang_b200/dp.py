@@ -371,7 +371,8 @@ class DataParallelProgram:
     def __init__(self, ast: list, env: Optional[dict], comm: Communicator, *, device: int,
                  feeds: Dict[str, np.ndarray], fetch: Optional[Sequence[str]] = None,
                  sharded: Sequence[str] = ("x", "t"), use_graphs: bool = True,
-                 bucket_bytes: Optional[int] = BUCKET_BYTES, fuse_head: bool = True):
+                 bucket_bytes: Optional[int] = BUCKET_BYTES, fuse_head: bool = True,
+                 fuse_colsum: bool = True):
         self.comm = comm
         gshapes = complete_env(ast, env or {})
         self.derived = batch_derived(ast, sharded)
@@ -393,7 +394,7 @@ class DataParallelProgram:
 
         self.program = Program(ast, None, device=device, feeds=feeds, fetch=fetch, shapes=local,
                                divisors=divisors, grad_hook=hook, use_graphs=use_graphs,
-                               fuse_head=fuse_head)
+                               fuse_head=fuse_head, fuse_colsum=fuse_colsum)
 
     def run(self):
         return self.program.run()

@@ -31,7 +31,7 @@ from .autograd import BackwardPlanner, Node, grad_name
 from .dataio import check_shape, load_data_file
 from .epilogue import fuse_gemm_epilogues
 from .head import fuse_classifier_head
-from .pairs import plan_gemm_pairs
+from .pairs import fuse_bias_colsums, plan_gemm_pairs
 from .kernel_generator import KernelGenerator
 from .shapes import Shape, broadcast, complete_env, expr_inputs, numel
 from .steps import EW, Copy, LibCall, Memset0, RegionStep, Step, fuse, kinfo_to_step
@@ -234,6 +234,7 @@ class Program:
                  feeds: Optional[Dict[str, np.ndarray]] = None, fetch: Optional[Iterable[str]] = None,
                  load_files: Optional[Dict[str, np.ndarray]] = None, record: str = "extended",
                  use_graphs: bool = True, fuse_ops: bool = True, fuse_head: bool = True,
+                 fuse_colsum: bool = True,
                  save_dir: Optional[str] = None,
                  shapes: Optional[Dict[str, Shape]] = None, divisors: Optional[dict] = None,
                  grad_hook=None, semantics: str = "reference"):
@@ -250,6 +251,7 @@ class Program:
         self.use_graphs = use_graphs
         self.fuse_ops = fuse_ops
         self.fuse_head = fuse_head  # classifier-head fusion (head.py), with fuse_ops
+        self.fuse_colsum = fuse_colsum  # bias sums folded into pair steps (pairs.py)
         self.save_dir = Path(save_dir) if save_dir else Path.cwd()
         self.divisors = divisors or {}
         self.grad_hook = grad_hook  # (program, exposed grads, backward steps) -> backward steps
@@ -453,6 +455,8 @@ class Program:
             if self.fuse_head:
                 fuse_classifier_head(self)
             plan_gemm_pairs(self)
+            if self.fuse_colsum:
+                fuse_bias_colsums(self)
         live = set(self.shapes) if self.fetch is None else set(self.fetch)
         live |= set(self.initial)
         live |= {sv["tensor"] for sv in self.saves}
@@ -572,6 +576,8 @@ class Program:
                 need = max(need, L.tl_reduce_full_scratch_bytes(a[0][1], a[3][1]))
             elif f == "tl_layer_norm_cols":
                 need = max(need, L.tl_norm_cols_scratch_bytes(a[2][1], a[3][1]))
+            elif f == "tl_gemm_pair_prepare_colsum":
+                need = max(need, L.tl_gemm_pair_colsum_scratch_bytes(a[2][1], a[3][1]))
             elif f in ("tl_mse_loss", "tl_cross_entropy"):
                 need = max(need, L.tl_loss_scratch_bytes(1))
         return int(need)

@@ -130,3 +130,60 @@ def added_after(lst: list, w) -> int:
             lst[i + n].fname == "tl_gemm_pair_prepare":
         n += 1
     return n
+
+
+def fuse_bias_colsums(P) -> int:
+    """Fold a bias gradient into the pair step of the same gradient.
+
+    A linear layer's backward sums dY over rows for db (``tl_reduce_cols``,
+    autograd.py:619-646) and converts the same dY into pairs for its dW and
+    dX products.  Where the pair step of X is followed, in the same step
+    list, by the row sum of X -- with nothing in between writing X or
+    touching the sum's output -- the pair step also writes the sum
+    (``tl_gemm_pair_prepare_colsum``: one read of X instead of two) and the
+    sum's own step is dropped.  Returns the number of sums folded."""
+    from .engine import _Loop
+
+    total = 0
+    for loop in (s for s in P.phase_pre if isinstance(s, _Loop)):
+        for lst in (loop.pre, loop.bw, loop.post, loop.rebind):
+            total += _fold_list(P, lst)
+    return total
+
+
+def _fold_list(P, lst: list) -> int:
+    folded = 0
+    i = 0
+    while i < len(lst):
+        st = lst[i]
+        if not (isinstance(st, LibCall) and st.fname == "tl_gemm_pair_prepare"):
+            i += 1
+            continue
+        X, ld, rows, cols = st.args[0][1], st.args[1][1], st.args[2][1], st.args[3][1]
+        j = next((k for k in range(i + 1, len(lst))
+                  if isinstance(lst[k], LibCall) and lst[k].fname == "tl_reduce_cols"
+                  and lst[k].args[1] == ("ptr", X)), None)
+        if j is None or ld != cols or cols > 8192:
+            i += 1
+            continue
+        red = lst[j]
+        a = red.args
+        if (a[0] != ("int", rt.RED_SUM) or a[2][0] != "ptr" or a[3] != ("int", rows)
+                or a[4] != ("int", cols)):
+            i += 1
+            continue
+        out = a[2][1]
+        between = lst[i + 1:j]
+        if any(X in b.writes or out in b.writes or out in b.reads for b in between):
+            i += 1
+            continue
+        if out in P.alias or out in P.alias.values():
+            i += 1
+            continue
+        lst[i] = LibCall(st.label + "+colsum:" + out, "tl_gemm_pair_prepare_colsum",
+                         list(st.args) + [("ptr", out), ("scratch",), ("scratch_bytes",)],
+                         list(st.reads), list(st.writes) + [out])
+        del lst[j]
+        folded += 1
+        i += 1
+    return folded

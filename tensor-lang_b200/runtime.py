@@ -117,6 +117,10 @@ _SIGS = [
     ("tl_gemm_tc_plan", c_int, [c_int64, c_int64, c_int64, ctypes.POINTER(c_int)]),
     ("tl_gemm_pair_prepare", c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
                                      c_void_p, c_int, c_void_p]),
+    ("tl_gemm_pair_colsum_scratch_bytes", ctypes.c_size_t, [c_int64, c_int64]),
+    ("tl_gemm_pair_prepare_colsum", c_int, [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_int,
+                                            c_void_p, c_int, c_void_p, c_void_p, ctypes.c_size_t,
+                                            c_void_p]),
     ("tl_gemm_uses_pairs", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_int64, c_int64]),
     ("tl_gemm_path", c_int, [c_int, c_int, c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p,
                              c_int64, c_void_p, c_int64]),

@@ -58,7 +58,8 @@ class EW(Step):
 class LibCall(Step):
     """A libtlb200 entry point.
 
-    args: ("ptr", name) | ("int", v) | ("float", v) | ("scratch",) | ("null",)
+    args: ("ptr", name) | ("int", v) | ("float", v) | ("scratch",) | ("scratch_bytes",)
+          | ("null",)
     The stream argument is appended.
     """
 
@@ -80,6 +81,8 @@ class LibCall(Step):
                 vals.append(c_float(a[1]))
             elif k == "scratch":
                 vals.append(c_void_p(P.scratch_ptr))
+            elif k == "scratch_bytes":
+                vals.append(ctypes.c_size_t(P.scratch.nbytes))
             elif k == "null":
                 vals.append(c_void_p(None))
             elif k == "handle":

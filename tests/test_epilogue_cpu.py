@@ -98,10 +98,13 @@ def test_operand_pairs_planned_once_per_value():
     assert sorted(loop.hoisted[0].writes) == ["__pair_x_hoist_k0", "__pair_x_hoist_m0"]
     body = loop.body()
     labels = [s.label for s in body]
-    prep = {s.label: s for s in body if getattr(s, "fname", "") == "tl_gemm_pair_prepare"}
+    prep = {s.label.split("+colsum")[0]: s for s in body
+            if getattr(s, "fname", "").startswith("tl_gemm_pair_prepare")}
+    labels = [lab.split("+colsum")[0] for lab in labels]
     assert sorted(prep) == ["pairs:a1", "pairs:h1_grad", "pairs:h2_grad"]
     # both layouts from one read where two roles use the value
-    assert len(prep["pairs:a1"].writes) == 2 and len(prep["pairs:h2_grad"].writes) == 2
+    pair_writes = {k: [w for w in st.writes if w.startswith("__pair_")] for k, st in prep.items()}
+    assert len(pair_writes["pairs:a1"]) == 2 and len(pair_writes["pairs:h2_grad"]) == 2
     # each pair step directly follows the step that writes its tensor
     for lab, st in prep.items():
         x = lab.split(":", 1)[1]
@@ -114,6 +117,40 @@ def test_operand_pairs_planned_once_per_value():
                      s.args[10][1] if s.args[10][0] == "ptr" else None):
             assert name is None or name.startswith("__pair_")
     assert not any("W2" in w for s in prep.values() for w in s.writes)
+
+
+def test_bias_sums_fold_into_pair_steps():
+    """pairs.py fuse_bias_colsums: db2 and db1 (the row sums of h2_grad and
+    h1_grad) are written by the pair steps of those gradients, one read of
+    each instead of two; a1's pair step has no sum to take; with
+    fuse_colsum=False the sums keep their own steps."""
+    tl = load_backend()
+    pr = tl.programs
+    kw = dict(B=4096, I=1024, H=4096, C=10)
+    P = tl.Program(pr.mlp3_train(epochs=2, **kw), None, fetch=["loss", "W3"])
+    P._fuse_all()
+    body = P.loops[0].body()
+    folded = {s.args[8][1]: s for s in body
+              if getattr(s, "fname", "") == "tl_gemm_pair_prepare_colsum"}
+    assert sorted(folded) == ["b1_grad", "b2_grad"]
+    assert folded["b2_grad"].args[0] == ("ptr", "h2_grad")
+    assert folded["b1_grad"].args[0] == ("ptr", "h1_grad")
+    for out, st in folded.items():
+        assert out in st.writes and st.args[9:] == [("scratch",), ("scratch_bytes",)]
+    sums = [s for s in body if getattr(s, "fname", "") == "tl_reduce_cols"]
+    assert [s.args[2][1] for s in sums] == ["b3_grad"]   # the head's db: no pair step
+    # the folded sum is written before every reader of it
+    names = [s.label for s in body]
+    for out, st in folded.items():
+        i = body.index(st)
+        assert not any(out in b.reads for b in body[:i])
+    Q = tl.Program(pr.mlp3_train(epochs=2, **kw), None, fetch=["loss", "W3"], fuse_colsum=False)
+    Q._fuse_all()
+    qb = Q.loops[0].body()
+    assert not any(getattr(s, "fname", "") == "tl_gemm_pair_prepare_colsum" for s in qb)
+    assert sorted(s.args[2][1] for s in qb if getattr(s, "fname", "") == "tl_reduce_cols") == [
+        "b1_grad", "b2_grad", "b3_grad"]
+    assert names  # labels computed
 
 
 def test_no_operand_pairs_under_the_three_tf32_scheme():
