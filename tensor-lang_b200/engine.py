@@ -576,8 +576,6 @@ class Program:
                 need = max(need, L.tl_reduce_full_scratch_bytes(a[0][1], a[3][1]))
             elif f == "tl_layer_norm_cols":
                 need = max(need, L.tl_norm_cols_scratch_bytes(a[2][1], a[3][1]))
-            elif f == "tl_gemm_pair_prepare_colsum":
-                need = max(need, L.tl_gemm_pair_colsum_scratch_bytes(a[2][1], a[3][1]))
             elif f in ("tl_mse_loss", "tl_cross_entropy"):
                 need = max(need, L.tl_loss_scratch_bytes(1))
         return int(need)

@@ -132,6 +132,9 @@ def added_after(lst: list, w) -> int:
     return n
 
 
+PARTIALS = "__colsum_partials"
+
+
 def fuse_bias_colsums(P) -> int:
     """Fold a bias gradient into the pair step of the same gradient.
 
@@ -141,7 +144,11 @@ def fuse_bias_colsums(P) -> int:
     list, by the row sum of X -- with nothing in between writing X or
     touching the sum's output -- the pair step also writes the sum
     (``tl_gemm_pair_prepare_colsum``: one read of X instead of two) and the
-    sum's own step is dropped.  Returns the number of sums folded."""
+    sum's own step is dropped.  Its per-block partial sums go to a buffer of
+    their own (``__colsum_partials``, shared by these steps, which run one
+    after another on the program's stream), not to the program's scratch,
+    whose counters the reduction and loss kernels keep at zero between
+    calls.  Returns the number of sums folded."""
     from .engine import _Loop
 
     total = 0
@@ -180,9 +187,12 @@ def _fold_list(P, lst: list) -> int:
         if out in P.alias or out in P.alias.values():
             i += 1
             continue
+        floats = (int(rt.lib().tl_gemm_pair_colsum_scratch_bytes(rows, cols)) + 3) // 4
+        have = P.shapes.get(PARTIALS, (0,))[0]
+        P.shapes[PARTIALS] = (max(have, floats),)
         lst[i] = LibCall(st.label + "+colsum:" + out, "tl_gemm_pair_prepare_colsum",
-                         list(st.args) + [("ptr", out), ("scratch",), ("scratch_bytes",)],
-                         list(st.reads), list(st.writes) + [out])
+                         list(st.args) + [("ptr", out), ("ptr", PARTIALS), ("bytes", PARTIALS)],
+                         list(st.reads), list(st.writes) + [out, PARTIALS])
         del lst[j]
         folded += 1
         i += 1

@@ -58,7 +58,7 @@ class EW(Step):
 class LibCall(Step):
     """A libtlb200 entry point.
 
-    args: ("ptr", name) | ("int", v) | ("float", v) | ("scratch",) | ("scratch_bytes",)
+    args: ("ptr", name) | ("int", v) | ("float", v) | ("scratch",) | ("bytes", name)
           | ("null",)
     The stream argument is appended.
     """
@@ -81,8 +81,8 @@ class LibCall(Step):
                 vals.append(c_float(a[1]))
             elif k == "scratch":
                 vals.append(c_void_p(P.scratch_ptr))
-            elif k == "scratch_bytes":
-                vals.append(ctypes.c_size_t(P.scratch.nbytes))
+            elif k == "bytes":
+                vals.append(ctypes.c_size_t(P.buffers[P.alias.get(a[1], a[1])].nbytes))
             elif k == "null":
                 vals.append(c_void_p(None))
             elif k == "handle":

@@ -136,7 +136,10 @@ def test_bias_sums_fold_into_pair_steps():
     assert folded["b2_grad"].args[0] == ("ptr", "h2_grad")
     assert folded["b1_grad"].args[0] == ("ptr", "h1_grad")
     for out, st in folded.items():
-        assert out in st.writes and st.args[9:] == [("scratch",), ("scratch_bytes",)]
+        # partial sums in a buffer of their own, not the program's scratch
+        assert out in st.writes and st.args[9:] == [("ptr", "__colsum_partials"),
+                                                    ("bytes", "__colsum_partials")]
+    assert P.shapes["__colsum_partials"][0] > 0
     sums = [s for s in body if getattr(s, "fname", "") == "tl_reduce_cols"]
     assert [s.args[2][1] for s in sums] == ["b3_grad"]   # the head's db: no pair step
     # the folded sum is written before every reader of it
