@@ -80,13 +80,15 @@ def test_folded_training_is_bit_identical(B, I, H, epochs):
     """The program with its relu / relu-VJP passes folded into GEMM epilogues,
     its operand pairs prepared once per value and its classifier head fused
     (head.py: forward product, softmax, the chained cross_entropy/softmax VJP
-    and the masked dX in one kernel) equals the unfused program bit for bit."""
+    and the masked dX in one kernel) equals the unfused program bit for bit.
+    (The bias sums folded into the pair steps add in another order and are
+    checked separately below.)"""
     tl = load_backend()
     pr = tl.programs
     ast = pr.mlp3_train(B=B, I=I, H=H, C=10, epochs=epochs)
     feeds = pr.mlp3_inputs(B=B, I=I, H=H, C=10, seed=3)
     fetch = ["loss", "W1", "b1", "W2", "b2", "W3", "b3"]
-    fused = tl.Program(ast, None, feeds=feeds, fetch=fetch)
+    fused = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_colsum=False)
     a = fused.run()
     steps = fused._all_steps()
     fused.free()
@@ -99,6 +101,31 @@ def test_folded_training_is_bit_identical(B, I, H, epochs):
     b = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_ops=False).run()
     for k in fetch:
         assert np.array_equal(np.asarray(a[k]), np.asarray(b[k])), k
+
+
+@pytest.mark.parametrize("B,I,H,epochs", [(512, 64, 384, 3), (8192, 1024, 4096, 2),
+                                          (65536, 1024, 4096, 1)])
+def test_folded_bias_sums_match(B, I, H, epochs):
+    """With the bias gradients' row sums folded into the pair steps of the
+    same gradients (pairs.py fuse_bias_colsums; both sums are taken in double
+    and rounded once, in different orders), the loss and every parameter
+    match the program that keeps the separate sums: rel 1e-6 of max|value|
+    (in practice equal, a float step at most where a double sum rounds the
+    other way)."""
+    tl = load_backend()
+    pr = tl.programs
+    ast = pr.mlp3_train(B=B, I=I, H=H, C=10, epochs=epochs)
+    feeds = pr.mlp3_inputs(B=B, I=I, H=H, C=10, seed=3)
+    fetch = ["loss", "W1", "b1", "W2", "b2", "W3", "b3"]
+    P = tl.Program(ast, None, feeds=feeds, fetch=fetch)
+    a = P.run()
+    steps = P._all_steps()
+    P.free()
+    assert sum(getattr(s, "fname", "") == "tl_gemm_pair_prepare_colsum" for s in steps) == 2
+    b = tl.Program(ast, None, feeds=feeds, fetch=fetch, fuse_colsum=False).run()
+    for k in fetch:
+        x, y = np.asarray(a[k], np.float64), np.asarray(b[k], np.float64)
+        assert np.abs(x - y).max() <= 1e-6 * max(np.abs(y).max(), 1e-30), k
 
 
 @pytest.mark.parametrize("ta,tb", [(0, 0), (0, 1), (1, 0), (1, 1)])
