@@ -1254,8 +1254,10 @@ __global__ void __launch_bounds__(256) pair_both_kernel(const float* __restrict_
 // block accumulates, in double, the columns of its threads over the rows it
 // converts (rows blockIdx.x + k * gridDim.x) and writes them as one row of
 // `part` ([gridDim.x][C] doubles); colsum_finish_kernel adds those rows.
-// J: column steps of 2048 per thread (c_end <= 2048 * J).
-template <int J>
+// J: column steps of 2048 per thread (c_end <= 2048 * J); SUM false: the
+// pairs alone (pair_prepare's kernel for up to 8192 columns: the unrolled
+// column steps keep every step's loads of a row in flight together).
+template <int J, bool SUM>
 __global__ void __launch_bounds__(256) pair_colsum_kernel(const float* __restrict__ X, int64_t ld,
                                                           int64_t R, int64_t C,
                                                           __nv_bfloat16* __restrict__ pk,
@@ -1290,8 +1292,10 @@ __global__ void __launch_bounds__(256) pair_colsum_kernel(const float* __restric
 #pragma unroll
         for (int i = 0; i < 8; ++i) x[i] = (r < R && c + i < C) ? src[c + i] : 0.f;
       }
+      if constexpr (SUM) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) acc[j][i] += (double)x[i];  // padding adds zeros
+        for (int i = 0; i < 8; ++i) acc[j][i] += (double)x[i];  // padding adds zeros
+      }
       const uint4 hv = make_uint4(pack_bf16(x[0], x[1]), pack_bf16(x[2], x[3]),
                                   pack_bf16(x[4], x[5]), pack_bf16(x[6], x[7]));
       const uint4 lv = make_uint4(pack_bf16(lo_of(x[0], lo_mode), lo_of(x[1], lo_mode)),
@@ -1309,6 +1313,7 @@ __global__ void __launch_bounds__(256) pair_colsum_kernel(const float* __restric
       }
     }
   }
+  if constexpr (!SUM) return;
   double* prow = part + (int64_t)blockIdx.x * C;
 #pragma unroll
   for (int j = 0; j < J; ++j) {
@@ -1694,22 +1699,40 @@ int64_t pair_bytes(int64_t rows, int64_t cols, int layout) {
   return -1;
 }
 
-int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
-                 int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st) {
-  const int64_t r_end = mnmajor ? (rows + 31) / 32 * 32 : rows;
-  const int64_t cap = 8LL * sm_count();
-  pair_both_kernel<<<(unsigned)(r_end < cap ? r_end : cap), 256, 0, st>>>(
-      X, ld, rows, cols, reinterpret_cast<__nv_bfloat16*>(kmajor), k_lo_first,
-      reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first, g_scheme == kSchemeBF16X3 ? 1 : 0);
-  return after_launch();
-}
-
 // Blocks of the pair pre-pass for rows x cols (and so rows of the column-sum
 // partials it writes).
 int64_t pair_grid(int64_t rows, bool mnmajor) {
   const int64_t r_end = mnmajor ? (rows + 31) / 32 * 32 : rows;
   const int64_t cap = 8LL * sm_count();
   return r_end < cap ? r_end : cap;
+}
+
+int pair_prepare(const float* X, int64_t ld, int64_t rows, int64_t cols, void* kmajor,
+                 int k_lo_first, void* mnmajor, int m_lo_first, cudaStream_t st) {
+  const int64_t c_end = kmajor ? (cols + 31) / 32 * 32 : (cols + 7) / 8 * 8;
+  if (c_end <= 4 * 2048) {
+    auto* pk = reinterpret_cast<__nv_bfloat16*>(kmajor);
+    auto* pm = reinterpret_cast<__nv_bfloat16*>(mnmajor);
+    const int lo = g_scheme == kSchemeBF16X3 ? 1 : 0;
+    const int64_t g = pair_grid(rows, mnmajor != nullptr);
+    auto launch = [&](auto kern) -> int {
+      int per_sm = 0;
+      TL_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, 256, 0));
+      const int64_t gg = std::min<int64_t>(g, (int64_t)std::max(per_sm, 1) * sm_count());
+      kern<<<(unsigned)gg, 256, 0, st>>>(X, ld, rows, cols, pk, k_lo_first, pm, m_lo_first, lo,
+                                         nullptr);
+      return after_launch();
+    };
+    if (c_end <= 2048) return launch(pair_colsum_kernel<1, false>);
+    if (c_end <= 4096) return launch(pair_colsum_kernel<2, false>);
+    return launch(pair_colsum_kernel<4, false>);
+  }
+  const int64_t r_end = mnmajor ? (rows + 31) / 32 * 32 : rows;
+  const int64_t cap = 8LL * sm_count();
+  pair_both_kernel<<<(unsigned)(r_end < cap ? r_end : cap), 256, 0, st>>>(
+      X, ld, rows, cols, reinterpret_cast<__nv_bfloat16*>(kmajor), k_lo_first,
+      reinterpret_cast<__nv_bfloat16*>(mnmajor), m_lo_first, g_scheme == kSchemeBF16X3 ? 1 : 0);
+  return after_launch();
 }
 
 size_t pair_colsum_scratch_bytes(int64_t rows, int64_t cols) {
@@ -1739,9 +1762,9 @@ int pair_prepare_colsum(const float* X, int64_t ld, int64_t rows, int64_t cols, 
     colsum_finish_kernel<<<(unsigned)((cols + 31) / 32), 1024, 0, st>>>(part, gg, cols, colsum);
     return after_launch();
   };
-  if (c_end <= 2048) return launch(pair_colsum_kernel<1>);
-  if (c_end <= 4096) return launch(pair_colsum_kernel<2>);
-  return launch(pair_colsum_kernel<4>);
+  if (c_end <= 2048) return launch(pair_colsum_kernel<1, true>);
+  if (c_end <= 4096) return launch(pair_colsum_kernel<2, true>);
+  return launch(pair_colsum_kernel<4, true>);
 }
 
 // The launch run_tiles makes for an M x N x K product on the tensor cores
