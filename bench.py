@@ -71,6 +71,11 @@ def set_tile_schedule(tl, name):
                      "tile schedule")
 
 
+def set_store_path(tl, name):
+    tl.runtime.check(tl.runtime.lib().tl_gemm_set_store_path(1 if name == "tma" else 0, None),
+                     "store path")
+
+
 def peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -573,6 +578,7 @@ def run_ours(args, rank, world, local):
     rt = tl.runtime
     set_gemm_scheme(tl, args.gemm_scheme)
     set_tile_schedule(tl, args.tile_schedule)
+    set_store_path(tl, args.store_path)
     from tensor_lang_b200 import dp
 
     dev = local
@@ -695,6 +701,7 @@ def run_micro(args):
     st = dev.stream
     set_gemm_scheme(tl, args.gemm_scheme)
     set_tile_schedule(tl, args.tile_schedule)
+    set_store_path(tl, args.store_path)
     hbm, bf16, _, src = peaks()
     reps = args.steps
     if args.micro == "reductions":
@@ -786,6 +793,9 @@ def main():
                          "work of eight)")
     ap.add_argument("--gemm-scheme", choices=sorted(GEMM_SCHEMES), default="bf16x3",
                     help="tensor-core operand scheme of the fp32 GEMMs")
+    ap.add_argument("--store-path", choices=("tma", "rows"), default="tma",
+                    help="CTA-pair GEMM epilogue: TMA stores of staged 32x32 slabs, or each "
+                         "lane storing its own row")
     ap.add_argument("--tile-schedule", choices=sorted(TILE_SCHEDULES), default="auto",
                     help="CTA-pair GEMM tile schedule: static groups, dynamic (running "
                          "clusters take pending clusters' tiles), or auto (the library's choice "

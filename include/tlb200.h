@@ -344,6 +344,16 @@ int  tl_gemm_set_cta_pair(int enable, int* previous);
  * every schedule.  *previous (if non-null) receives the setting that was in
  * force. */
 int  tl_gemm_set_tile_schedule(int dynamic, int* previous);
+/* How the CTA-pair kernel's epilogue writes its tiles (no reference
+ * counterpart).  tma = 1 (default): each epilogue warp stages 32 x 32 slabs of
+ * its rows in shared memory (128-byte swizzle) and stores them with TMA,
+ * whole 128-byte row segments at a time, wherever the output has a 16-byte
+ * aligned base and rows (split-K partial sums too); accumulate and other
+ * layouts keep the per-row stores.  tma = 0: every lane stores its own row
+ * (16 bytes per lane per instruction, 32 rows per warp store).  Results are
+ * bit-identical either way.  *previous (if non-null) receives the setting
+ * that was in force. */
+int  tl_gemm_set_store_path(int tma, int* previous);
 /* ---- classifier head of a training step, fused ---------------------------
  * linear (kernel_generator.py:1584-1661) with N <= 16 outputs, row softmax
  * (:564-640) and cross_entropy (:1816-1885), and their backward:

@@ -33,6 +33,7 @@ void gemm_set_split_mode(int mode);
 int gemm_set_scheme(int scheme);
 int gemm_set_cta_pair(int enable);
 int gemm_set_tile_dynamic(int enable);
+int gemm_set_tma_store(int mode);
 int gemm_small(int ta, int tb, int64_t M, int64_t N, int64_t K, const float* A, int64_t lda,
                const float* B, int64_t ldb, float* C, int64_t ldc, const float* bias,
                int accumulate, int epilogue, const float* mask, int64_t ldm, cudaStream_t st);
@@ -267,6 +268,13 @@ int tl_gemm_set_cta_pair(int enable, int* previous) {
 int tl_gemm_set_tile_schedule(int dynamic, int* previous) {
   if (dynamic < 0 || dynamic > 2) return TL_ERR_INVALID_ARG;
   const int prev = tl::gemm_set_tile_dynamic(dynamic);
+  if (previous) *previous = prev;
+  return TL_OK;
+}
+
+int tl_gemm_set_store_path(int tma, int* previous) {
+  if (tma < 0 || tma > 1) return TL_ERR_INVALID_ARG;
+  const int prev = tl::gemm_set_tma_store(tma);
   if (previous) *previous = prev;
   return TL_OK;
 }

@@ -53,6 +53,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstring>
 #include <mutex>
 #include <vector>
 
@@ -277,6 +278,7 @@ struct Params {
   float* partial;     // [splits][M][N] raw sums when splits > 1
   int tpc = 1;        // CTA-pair kernel: tiles each cluster computes in turn
   int clc = 0;        // CTA-pair kernel: take pending clusters' tiles (cluster launch control)
+  int tma_store = 0;  // CTA-pair kernel: results leave through shared memory and TMA stores
 };
 
 // Split-K partial of one thread's BN/2 columns of row `row` (no epilogue).
@@ -590,7 +592,12 @@ constexpr int STAGES2 = 3;
 constexpr int HB = 128;                            // B rows (N) held per CTA
 constexpr int B_HALF = HB * BK * 4;                // 16 KB
 constexpr int STAGE2_BYTES = 2 * A_TILE + 2 * B_HALF;  // 64 KB per CTA
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 512;
+// Epilogue staging for TMA stores: one 32 x 32 fp32 tile (4 KB, 128-byte
+// swizzle) per epilogue warp.
+constexpr int STG_TILE = 32 * 32 * 4;
+constexpr int STG_BYTES = EPI_WARPS * STG_TILE;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + STG_BYTES + 1024 + 512;
+static_assert(SMEM2_BYTES <= 227 * 1024, "CTA-pair kernel shared memory");
 // The BF16X3 scheme stages only the two pair tiles (32 KB per CTA), so twice
 // as many stages fit in the same shared memory.
 template <int SCHEME>
@@ -645,6 +652,103 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       "l"((uint64_t)map), "r"(bar), "r"(c0), "r"(c1)
       : "memory");
 }
+// TMA stores of a staged 32 x 32 fp32 tile (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];"
+               ::"l"((uint64_t)map), "r"(src), "r"(c0), "r"(c1)
+               : "memory");
+}
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, uint32_t src, int c0, int c1,
+                                             int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"((uint64_t)map), "r"(src), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// the staging tile may be written again once earlier stores have read it
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+__device__ __forceinline__ void st_shared_v4(uint32_t a, float x, float y, float z, float w) {
+  asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(a), "f"(x), "f"(y), "f"(z), "f"(w)
+               : "memory");
+}
+
+// store_row's bias, relu and relu-VJP mask, in place and in the same order
+// (so the stored values are the same bits), for a row that exists.
+__device__ __forceinline__ void epi_apply(const Params& p, int row, int nb0, float (&sum)[BN / 2]) {
+  if (row >= p.M || nb0 >= p.N) return;
+  if (p.bias) {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j)
+      if (nb0 + j < p.N) sum[j] += __ldg(&p.bias[nb0 + j]);
+  }
+  if (p.epilogue == TL_EPI_RELU) {
+#pragma unroll
+    for (int j = 0; j < BN / 2; ++j) sum[j] = fmaxf(0.f, sum[j]);
+  }
+  if (p.mask) {
+    const float* mrow = p.mask + (int64_t)row * p.ldm + nb0;
+    if (nb0 + BN / 2 <= p.N && (p.ldm % 4 == 0) && (((uintptr_t)p.mask & 15) == 0)) {
+#pragma unroll
+      for (int j = 0; j < BN / 8; ++j) {
+        const float4 q = __ldg(reinterpret_cast<const float4*>(mrow) + j);
+        sum[4 * j] = __fmul_rn(sum[4 * j], q.x > 0.f ? 1.f : 0.f);
+        sum[4 * j + 1] = __fmul_rn(sum[4 * j + 1], q.y > 0.f ? 1.f : 0.f);
+        sum[4 * j + 2] = __fmul_rn(sum[4 * j + 2], q.z > 0.f ? 1.f : 0.f);
+        sum[4 * j + 3] = __fmul_rn(sum[4 * j + 3], q.w > 0.f ? 1.f : 0.f);
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < BN / 2; ++j)
+        if (nb0 + j < p.N) sum[j] = __fmul_rn(sum[j], mrow[j] > 0.f ? 1.f : 0.f);
+    }
+  }
+}
+
+// A warp's 32 rows x BN/2 columns (lane = row) leave in 32-column slabs:
+// each lane writes its row of the slab into the warp's staging tile (16-byte
+// chunk j of row r at chunk j ^ (r & 7): the tensor map's 128-byte swizzle,
+// and no bank conflicts), then lane 0 stores the tile with TMA.  Rows past M
+// and columns past N are clipped by the tensor map; slabs that start past
+// them are skipped.  With `split` >= 0 the map is the 3-D split-K partial
+// buffer [split][M][N].
+__device__ __forceinline__ void tma_store_rows(const CUtensorMap* map, uint32_t stg, int lane,
+                                               int row0, int nb0, int M, int N, int split,
+                                               const float (&sum)[BN / 2]) {
+  if (row0 >= M) return;
+#pragma unroll
+  for (int s = 0; s < BN / 64; ++s) {
+    const int c0 = nb0 + 32 * s;
+    if (c0 >= N) break;
+    if (lane == 0) bulk_wait_read();
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t a = stg + (uint32_t)lane * 128u + ((uint32_t)(j ^ (lane & 7)) << 4);
+      st_shared_v4(a, sum[32 * s + 4 * j], sum[32 * s + 4 * j + 1], sum[32 * s + 4 * j + 2],
+                   sum[32 * s + 4 * j + 3]);
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if (split >= 0)
+        tma_store_3d(map, stg, c0, row0, split);
+      else
+        tma_store_2d(map, stg, c0, row0);
+      bulk_commit();
+    }
+  }
+}
+
 __device__ __forceinline__ void mma2_tf32(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
                                           uint32_t idesc, uint32_t accumulate) {
   asm volatile(
@@ -731,13 +835,14 @@ template <int TA, int TB, int SCHEME>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmAx,
                     const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmBx,
-                    Params p) {
+                    const __grid_constant__ CUtensorMap tmC, Params p) {
   constexpr bool PAIR = SCHEME != kScheme3xTF32;  // bf16 pair tiles
   constexpr bool X3 = Ring2<SCHEME>::X3;          // pair tiles only, no fp32 tiles
   constexpr int NST = Ring2<SCHEME>::kStages, SBYTES = Ring2<SCHEME>::kBytes;
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem = (unsigned char*)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-  uint64_t* bars = (uint64_t*)(smem + NST * SBYTES);
+  unsigned char* stage_out = smem + NST * SBYTES;  // [EPI_WARPS][STG_TILE], 1024-aligned
+  uint64_t* bars = (uint64_t*)(stage_out + STG_BYTES);
   uint64_t* full = bars;                // [NST] loads of both CTAs -> leader's MMA
   uint64_t* empty = bars + NST;         // [NST] MMA -> each CTA's producer
   uint64_t* acc_full = bars + 2 * NST;  // [2] MMA -> each CTA's epilogue
@@ -1010,13 +1115,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(free0 + 8u * (uint32_t)b);
       }
+      ok = __all_sync(0xffffffffu, ok);  // the slab stores below are warp-wide
       if (ok) {
         const Tile2 tt = tile2_of(p, g, m_tiles, n_tiles, nk_all);
         const int row = tt.m0 + 128 * (int)rank + quarter * 32 + lane;
-        if (p.splits > 1)
-          store_partial(p, tt.split, row, tt.n0 + half * (BN / 2), sum);
-        else
-          store_row(p, row, tt.n0 + half * (BN / 2), sum);
+        const int nb0 = tt.n0 + half * (BN / 2);
+        if (p.tma_store) {
+          if (p.splits == 1) epi_apply(p, row, nb0, sum);
+          tma_store_rows(&tmC, smem_u32(stage_out + e * STG_TILE), lane, row - lane, nb0, p.M, p.N,
+                         p.splits > 1 ? tt.split : -1, sum);
+        } else if (p.splits > 1) {
+          store_partial(p, tt.split, row, nb0, sum);
+        } else {
+          store_row(p, row, nb0, sum);
+        }
       }
     }
     if (!ok || !p.clc) break;
@@ -1025,6 +1137,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     __syncwarp();
     if (grp < 0) break;
     }
+    // the staging tiles stay allocated until every TMA store has read them
+    if (p.tma_store && lane == 0) bulk_wait_all();
+    __syncwarp();
   }
   fence_before();
   cluster_sync_all();  // neither CTA releases TMEM or exits while the pair is still working
@@ -1395,6 +1510,18 @@ bool make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int
 
 // 2-D bf16 tensor map over a pair matrix [rows][2*kp]: 64-wide boxes (128 B),
 // 128-byte swizzle, K-major.
+// 3-D fp32 tensor map over split-K partial sums [splits][M][N]: 32 x 32 x 1
+// boxes, 128-byte swizzle (the epilogue's staging layout).
+bool make_partial_map(CUtensorMap* m, const float* base, int64_t splits, int64_t M, int64_t N) {
+  cuuint64_t dims[3] = {(cuuint64_t)N, (cuuint64_t)M, (cuuint64_t)splits};
+  cuuint64_t strides[2] = {(cuuint64_t)N * 4, (cuuint64_t)(M * N) * 4};
+  cuuint32_t box[3] = {32, 32, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, (void*)base, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 bool make_pair_map(CUtensorMap* m, const __nv_bfloat16* base, int64_t rows, int64_t kp,
                    uint32_t box_outer) {
   cuuint64_t dims[2] = {(cuuint64_t)(2 * kp), (cuuint64_t)rows};
@@ -1451,6 +1578,9 @@ int g_tiles_per_cluster = 4;  // upper bound on the tiles one CTA pair computes 
 // control), so an SM pair computes tiles back to back until none are left;
 // 2 (default) dynamic where it measured faster (use_dynamic)
 int g_tile_dynamic = 2;
+// CTA-pair epilogue: 1 (default) TMA stores from shared memory where the
+// output allows a tensor map, 0 every lane stores its own row
+int g_tma_store = 1;
 
 // Tiles per cluster for a CTA-pair launch of `tiles` tiles: each cluster
 // launch pays a prologue (barrier set-up, TMEM allocation, pipeline fill) and
@@ -1520,7 +1650,19 @@ int run_tiles(bool two, const CUtensorMap& ma, const CUtensorMap& max_, const CU
       TL_TRY(workspace((size_t)splits * M * N, &part, st, g_ws_partial));
       q.partial = part;
     }
-    kern<<<(unsigned)(2 * launched), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, q);
+    // results through shared memory and TMA stores where the output's layout
+    // allows a tensor map (16-byte aligned base and rows); accumulate keeps
+    // the read-modify-write stores
+    CUtensorMap mc;
+    memset(&mc, 0, sizeof(mc));
+    if (g_tma_store && !q.accumulate) {
+      if (splits > 1)
+        q.tma_store = (N % 4 == 0) && make_partial_map(&mc, q.partial, splits, M, N) ? 1 : 0;
+      else
+        q.tma_store = (q.ldc % 4 == 0) && ((((uintptr_t)q.C) & 15) == 0) &&
+                      make_map(&mc, q.C, M, N, q.ldc, 32, 32, false) ? 1 : 0;
+    }
+    kern<<<(unsigned)(2 * launched), THREADS, SMEM2_BYTES, st>>>(ma, max_, mb, mbx, mc, q);
     if (splits > 1) {
       TL_TRY(after_launch());
       const int64_t units = (N % 4 == 0) ? M * N / 4 : M * N;
@@ -1796,6 +1938,12 @@ void gemm_set_split_mode(int mode) { g_split_mode = mode; }
 int gemm_set_cta_pair(int enable) {
   const int prev = g_cta_pair;
   g_cta_pair = enable ? 1 : 0;
+  return prev;
+}
+
+int gemm_set_tma_store(int mode) {
+  const int prev = g_tma_store;
+  g_tma_store = mode ? 1 : 0;
   return prev;
 }
 

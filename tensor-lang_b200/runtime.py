@@ -128,6 +128,7 @@ _SIGS = [
     ("tl_gemm_set_scheme", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_gemm_set_cta_pair", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_gemm_set_tile_schedule", c_int, [c_int, ctypes.POINTER(c_int)]),
+    ("tl_gemm_set_store_path", c_int, [c_int, ctypes.POINTER(c_int)]),
     ("tl_head_ce_ok", c_int, [c_int64, c_int64, c_int64, c_void_p, c_int64, c_void_p, c_int64]),
     ("tl_head_ce", c_int, [c_void_p, c_int64, c_void_p, c_int64, c_void_p, c_void_p, c_int,
                            c_void_p, c_float, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -138,3 +138,53 @@ def test_split_k_gemm(ta, tb, M, N, K, bias, acc, relu):
     out, ref, err = _masked(ta, tb, M, N, K, bias=bias, acc=acc, relu=relu)
     assert err == 0
     assert_close(out, ref, 1e-5, f"split-K {ta}{tb} {M}x{N}x{K}")
+
+
+class _StorePath:
+    """Select the CTA-pair epilogue's store path for a with-block."""
+
+    def __init__(self, tma):
+        self.tma = tma
+
+    def __enter__(self):
+        self.L = load_backend().runtime.lib()
+        self.prev = ctypes.c_int(-1)
+        assert self.L.tl_gemm_set_store_path(self.tma, ctypes.byref(self.prev)) == 0
+        return self
+
+    def __exit__(self, *exc):
+        self.L.tl_gemm_set_store_path(self.prev.value, None)
+        return False
+
+
+@pytest.mark.parametrize("ta,tb,M,N,K,bias,acc,relu,masked", [
+    (0, 0, 4096, 4096, 1024, True, False, True, False),   # the first layer's shape, scaled
+    (0, 1, 4096, 4096, 2048, False, False, False, True),  # dX with the relu-VJP mask
+    (1, 0, 1024, 4096, 8192, False, False, False, False),  # dW: K split 8 (partials by TMA)
+    (0, 0, 1000, 1000, 520, True, False, True, True),     # ragged rows and columns
+    (1, 1, 333, 260, 4096, True, False, False, False),    # ragged, split K
+    (0, 0, 600, 300, 256, True, True, True, False),       # accumulate: per-row stores
+    (0, 0, 515, 258, 512, True, False, True, False),      # N not a multiple of 4
+])
+def test_tma_store_epilogue_is_bit_identical(ta, tb, M, N, K, bias, acc, relu, masked):
+    """The CTA-pair epilogue's TMA stores (32 x 32 slabs staged in shared
+    memory, clipped at the edges; split-K partials through a 3-D map) give the
+    per-row stores' results bit for bit, with bias, relu, the relu-VJP mask
+    and accumulate, on ragged shapes; both within rel 1e-5 of float64."""
+    outs = []
+    for tma in (0, 1):
+        with _StorePath(tma):
+            if masked:
+                out, ref, err = _masked(ta, tb, M, N, K, bias=bias, acc=acc, relu=relu)
+            else:
+                from test_gpu_gemm import _run
+                out, ref, path, err = _run(ta, tb, M, N, K, bias=bias, acc=acc, relu=relu)
+                assert path == 0
+        assert err == 0
+        outs.append(out)
+    np.testing.assert_array_equal(outs[1], outs[0])
+    assert_close(outs[1], ref, 1e-5, f"TMA-store epilogue {ta}{tb} {M}x{N}x{K}")
+
+
+def test_store_path_rejects_unknown():
+    assert load_backend().runtime.lib().tl_gemm_set_store_path(2, None) != 0
