@@ -162,7 +162,7 @@ class _StorePath:
     (0, 1, 4096, 4096, 2048, False, False, False, True),  # dX with the relu-VJP mask
     (1, 0, 1024, 4096, 8192, False, False, False, False),  # dW: K split 8 (partials by TMA)
     (0, 0, 1000, 1000, 520, True, False, True, True),     # ragged rows and columns
-    (1, 1, 333, 260, 4096, True, False, False, False),    # ragged, split K
+    (1, 1, 336, 260, 4096, True, False, False, False),    # ragged, split K
     (0, 0, 600, 300, 256, True, True, True, False),       # accumulate: per-row stores
     (0, 0, 515, 258, 512, True, False, True, False),      # N not a multiple of 4
 ])
