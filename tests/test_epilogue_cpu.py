@@ -175,3 +175,50 @@ def test_no_operand_pairs_under_the_three_tf32_scheme():
     finally:
         L.tl_gemm_set_scheme(prev.value, None)
     assert prev.value == 2  # BF16X3 is the default
+
+
+def test_bias_sum_fold_needs_an_untouched_span():
+    """fuse_bias_colsums folds a row sum into the pair step of the same tensor
+    only when nothing between them writes the tensor or touches the sum, the
+    sum is a plain SUM over the tensor's full shape, and cols <= 8192."""
+    tl = load_backend()
+    from tensor_lang_b200 import pairs
+    from tensor_lang_b200.steps import LibCall
+    rt = tl.runtime
+
+    class _P:
+        alias: dict = {}
+
+        def __init__(self):
+            self.shapes = {}
+
+    def pair(rows=512, cols=256):
+        return LibCall("pairs:g", "tl_gemm_pair_prepare",
+                       [("ptr", "g"), ("int", cols), ("int", rows), ("int", cols),
+                        ("ptr", "__pk"), ("int", 0), ("ptr", "__pm"), ("int", 1)],
+                       ["g"], ["__pk", "__pm"])
+
+    def rsum(op=rt.RED_SUM, rows=512, cols=256, src="g"):
+        return LibCall("db:b", "tl_reduce_cols",
+                       [("int", op), ("ptr", src), ("ptr", "b"), ("int", rows), ("int", cols),
+                        ("scratch",)], [src], ["b"])
+
+    def other(reads=(), writes=()):
+        return LibCall("x", "tl_something", [], list(reads), list(writes))
+
+    cases = [
+        ([pair(), other(), rsum()], 1),                         # folds
+        ([pair(), other(reads=["b"]), rsum()], 0),              # the sum is read in between
+        ([pair(), other(writes=["b"]), rsum()], 0),             # ... or written
+        ([pair(), other(writes=["g"]), rsum()], 0),             # the tensor changes in between
+        ([pair(), rsum(op=rt.RED_MAX)], 0),                     # not a sum
+        ([pair(), rsum(rows=256)], 0),                          # another shape
+        ([pair(rows=64, cols=8200), rsum(rows=64, cols=8200)], 0),  # too wide
+    ]
+    for lst, want in cases:
+        P = _P()
+        got = pairs._fold_list(P, lst)
+        assert got == want, [s.label for s in lst]
+        if want:
+            assert [s.fname for s in lst] == ["tl_gemm_pair_prepare_colsum", "tl_something"]
+            assert "b" in lst[0].writes and P.shapes[pairs.PARTIALS][0] > 0
